@@ -1,0 +1,297 @@
+"""CPU oracle for the Bigger Bird v3 sparse-prefill path (TEST INFRASTRUCTURE ONLY).
+
+This module is a numpy restatement of the reference's algorithm. It exists so that the
+tests, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` leg of ``bench.py`` can check
+the CUDA path; the product (``utmist_bigger_bird_b200``) never imports it.
+
+What it restates (paths inside the reference project derkychen/utmist-bigger-bird):
+
+* ``rope``           -- ``modal_rd/attention.py:51-60`` (``rope_inplace``), i.e. Hugging Face
+                        ``apply_rotary_pos_emb`` / ``rotate_half`` (transformers, pinned 5.15.1 in
+                        ``modal_rd/app.py:24``; the formula is unchanged in 5.5): each op of
+                        ``x*cos + rotate_half(x)*sin`` rounds to the tensor dtype.
+* ``vertical_budget`` -- ``modal_rd/attention.py:63-67``.
+* ``route_query_positions`` -- ``modal_rd/attention.py:151-155`` (``torch.linspace`` in float32,
+                        truncated by ``.long()``; ATen's symmetric linspace formula).
+* ``route_scores`` / ``routes`` -- ``modal_rd/attention.py:143-174``: bf16/fp16 scores are the
+                        matmul output rounded to the input dtype, then ``.float() * scaling``,
+                        causal mask, fp32 softmax over all keys, mean (or max) over the routing
+                        queries, sink and window columns forced to -1, top-``budget`` sorted.
+* ``flash``          -- ``kernels/bigger_bird_flash_ref.py:10-52`` (same masks: sink, causal
+                        window, routed columns beyond the window, route groups, token mask;
+                        fully masked rows give 0), computed in fp32, optionally on a subset of
+                        query rows so long sequences stay tractable.
+* ``sparse_prefill`` -- ``modal_rd/attention.py:176-206`` (routes, optional ``vertical_scope``
+                        groups, main pass, exact tail overwriting the last ``exact_tail`` rows).
+
+Parity is pinned by ``tests/test_oracle_golden.py`` against vectors produced by the reference
+itself (``tests/golden/make_golden.py`` imports the reference read-only).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+__all__ = [
+    "bf16_round", "f16_round", "rounder", "rope", "vertical_budget", "route_query_positions",
+    "route_scores", "routes", "topk_sorted", "route_sets_match", "flash", "sparse_prefill",
+]
+
+
+# ----------------------------------------------------------------------------- rounding helpers
+
+def bf16_round(x):
+    """float32 -> float32 holding the bfloat16 round-to-nearest-even value (NaN kept)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    b = x.view(np.uint32).astype(np.uint64)
+    b = (b + 0x7FFF + ((b >> 16) & 1)) & 0xFFFF0000
+    out = b.astype(np.uint32).view(np.float32)
+    return np.where(np.isnan(x), x, out)
+
+
+def f16_round(x):
+    return np.asarray(x, dtype=np.float32).astype(np.float16).astype(np.float32)
+
+
+def rounder(dtype):
+    """Rounding applied by a torch op whose output dtype is ``dtype`` ("bf16", "f16", "f32")."""
+    if dtype == "bf16":
+        return bf16_round
+    if dtype == "f16":
+        return f16_round
+    if dtype == "f32":
+        return lambda a: np.asarray(a, dtype=np.float32)
+    raise ValueError(f"unknown dtype {dtype}")
+
+
+# ----------------------------------------------------------------------------- RoPE
+
+def rope(x, cos, sin, dtype):
+    """``x*cos + rotate_half(x)*sin`` with each op rounded to ``dtype``.
+
+    x: [..., T, D] float32 (values representable in ``dtype``); cos/sin: [T, D] float32
+    (already in ``dtype``). Restates ``modal_rd/attention.py:51-60`` (chunking there is
+    position-wise and does not change results)."""
+    rnd = rounder(dtype)
+    x = np.asarray(x, dtype=np.float32)
+    half = x.shape[-1] // 2
+    rot = np.concatenate([-x[..., half:], x[..., :half]], axis=-1)
+    return rnd(rnd(x * cos) + rnd(rot * sin))
+
+
+# ----------------------------------------------------------------------------- routing
+
+def vertical_budget(n, vertical, vertical_sqrt):
+    """``modal_rd/attention.py:63-67``."""
+    if vertical_sqrt > 0:
+        return int(math.ceil(vertical_sqrt * math.sqrt(n) / 64) * 64)
+    return vertical
+
+
+def route_query_positions(n, r, mode, sink, window):
+    """Routing query positions (``modal_rd/attention.py:151-155``).
+
+    "spread" restates ``torch.linspace(sink + window, n - 1, r).long()``: float32 endpoints,
+    ``step = (end - start) / (steps - 1)``, the first ``steps // 2`` values are
+    ``start + step * i`` and the rest ``end - step * (steps - 1 - i)``, then truncation."""
+    if mode == "spread":
+        start, end = np.float32(sink + window), np.float32(n - 1)
+        if r == 1:
+            vals = np.array([start], dtype=np.float32)
+        else:
+            step = np.float32((end - start) / np.float32(r - 1))
+            i = np.arange(r)
+            lo = start + step * i.astype(np.float32)
+            hi = end - step * (r - 1 - i).astype(np.float32)
+            vals = np.where(i < r // 2, lo, hi).astype(np.float32)
+        return vals.astype(np.int64)
+    if mode == "last":
+        return np.arange(n - r, n, dtype=np.int64)
+    raise ValueError("route_queries must be last or spread")
+
+
+def route_scores(q, k, *, scaling, sink, window, n_route=64, pool="mean", queries="last",
+                 dtype="bf16", qpos=None):
+    """Per-Q-head column scores ``col [H, n]`` (fp32) before top-k.
+
+    q: [H, n, d], k: [Hk, n, d] float32 arrays holding ``dtype`` values (post-RoPE).
+    ``modal_rd/attention.py:148-170``."""
+    q = np.asarray(q, dtype=np.float32)
+    k = np.asarray(k, dtype=np.float32)
+    H, n, d = q.shape
+    hk = k.shape[0]
+    g = H // hk
+    r = min(n_route, n)
+    if qpos is None:
+        qpos = route_query_positions(n, r, queries, sink, window)
+    qpos = np.asarray(qpos, dtype=np.int64)
+    rnd = rounder(dtype)
+    keypos = np.arange(n)
+    qpos_g = np.tile(qpos, g)
+    masked = keypos[None, :] > qpos_g[:, None]
+    col = np.zeros((H, n), dtype=np.float32)
+    for h in range(hk):
+        qa = q[h * g:(h + 1) * g][:, qpos, :].reshape(g * r, d)
+        s = (qa.astype(np.float64) @ k[h].astype(np.float64).T).astype(np.float32)
+        s = rnd(s) * np.float32(scaling)
+        s[masked] = -np.inf
+        m = s.max(-1, keepdims=True)
+        e = np.exp(s - m)
+        p = (e / e.sum(-1, keepdims=True, dtype=np.float32)).reshape(g, r, n)
+        if pool == "max":
+            pooled = p.max(1)
+        elif pool == "mean":
+            pooled = p.sum(1, dtype=np.float32) / np.float32(r)
+        else:
+            raise ValueError("route_pool must be mean or max")
+        col[h * g:(h + 1) * g] = pooled
+    col[:, :sink] = -1
+    col[:, n - window:] = -1          # Python slice semantics, as in the reference
+    return col
+
+
+def topk_sorted(col, budget):
+    """``col.topk(budget).indices.sort(-1).values.to(int32)``; ties resolved to lower index."""
+    H, n = col.shape
+    out = np.empty((H, budget), dtype=np.int32)
+    for h in range(H):
+        order = np.lexsort((np.arange(n), -col[h].astype(np.float64)))
+        out[h] = np.sort(order[:budget])
+    return out
+
+
+def routes(q, k, *, scaling, sink, window, vertical, vertical_sqrt=0.0, n_route=64, pool="mean",
+           queries="last", dtype="bf16", qpos=None, return_scores=False):
+    """``RDAttention.routes`` (``modal_rd/attention.py:143-174``) -> int32 [H, budget]."""
+    n = k.shape[-2]
+    budget = min(vertical_budget(n, vertical, vertical_sqrt), max(0, n - sink - window))
+    col = route_scores(q, k, scaling=scaling, sink=sink, window=window, n_route=n_route, pool=pool,
+                       queries=queries, dtype=dtype, qpos=qpos)
+    idx = topk_sorted(col, budget)
+    return (idx, col) if return_scores else idx
+
+
+def route_sets_match(got, want, col, tol=1e-6):
+    """True when every head's route set equals the oracle's, except indices whose oracle score
+    lies within ``tol`` of that head's ``budget``-th score (a tie at the selection boundary).
+
+    Returns (ok, n_swapped, worst_gap)."""
+    got = np.asarray(got)
+    want = np.asarray(want)
+    if got.shape != want.shape:
+        return False, -1, float("inf")
+    swapped, worst = 0, 0.0
+    for h in range(want.shape[0]):
+        a, b = set(got[h].tolist()), set(want[h].tolist())
+        diff = a ^ b
+        if not diff:
+            continue
+        if any(i < 0 or i >= col.shape[1] for i in diff):
+            return False, len(diff), float("inf")
+        kth = col[h, want[h]].min()
+        gap = max(abs(float(col[h, i]) - float(kth)) for i in diff)
+        worst = max(worst, gap)
+        swapped += len(diff) // 2
+        if gap > tol:
+            return False, swapped, worst
+    return True, swapped, worst
+
+
+# ----------------------------------------------------------------------------- attention
+
+def _kv_head(h, num_heads, kv_groups):
+    return (h // num_heads) * (num_heads // kv_groups) + (h % num_heads) // kv_groups
+
+
+def flash(q, k, v, indices, *, front=64, window=256, token_mask=None, num_heads=32, route_chunk=None,
+          kv_groups=1, scale=1.0, rows=None, heads=None):
+    """fp32 restatement of ``bigger_bird_flash_ref`` (``kernels/bigger_bird_flash_ref.py:10-52``).
+
+    q [BH, T, D], k/v [BH/kv_groups, N, D] (float32 arrays), indices [BH, G, K] or [BH, K]
+    (-1 = empty slot; out-of-range indices are treated as empty). ``rows`` selects query rows
+    (local indices into T) and ``heads`` selects query heads; the result is
+    ``[len(heads), len(rows), D]`` float32 (not rounded to the input dtype)."""
+    q = np.asarray(q, dtype=np.float32)
+    k = np.asarray(k, dtype=np.float32)
+    v = np.asarray(v, dtype=np.float32)
+    bh, t, d = q.shape
+    n = k.shape[1]
+    offset = n - t
+    if offset < 0:
+        raise ValueError("Key sequence must be at least as long as query sequence")
+    idx_all = np.asarray(indices)
+    if idx_all.ndim == 2:
+        idx_all = idx_all[:, None, :]
+    route_chunk = route_chunk or n
+    front = min(front, n)
+    rows = np.arange(t) if rows is None else np.asarray(rows, dtype=np.int64)
+    heads = np.arange(bh) if heads is None else np.asarray(heads, dtype=np.int64)
+    qs = rows + offset
+    kp = np.arange(n)
+    causal = kp[None, :] <= qs[:, None]
+    base = causal & ((kp[None, :] < front) | (kp[None, :] > qs[:, None] - window))
+    beyond = kp[None, :] < qs[:, None] - window + 1
+    group = qs // route_chunk
+    out = np.zeros((len(heads), len(rows), d), dtype=np.float32)
+    for oi, h in enumerate(heads):
+        kv = _kv_head(int(h), num_heads, kv_groups)
+        idx = idx_all[h].astype(np.int64)                         # [G, K]
+        routed = np.zeros((idx.shape[0], n + 1), dtype=bool)
+        valid = (idx >= 0) & (idx < n)
+        gi, _ = np.nonzero(valid)
+        routed[gi, idx[valid]] = True
+        routed = routed[:, :n][group]                               # [R, N]
+        mask = base | (routed & causal & (kp[None, :] >= front) & beyond)
+        if token_mask is not None:
+            b = int(h) // num_heads
+            mask &= np.asarray(token_mask[b], dtype=bool)[None, :]
+        s = (q[h, rows] @ k[kv].T) * np.float32(scale)
+        s = np.where(mask, s, -np.inf).astype(np.float32)
+        m = s.max(-1, keepdims=True)
+        m = np.where(np.isfinite(m), m, 0.0).astype(np.float32)
+        e = np.exp(s - m)
+        den = e.sum(-1, keepdims=True, dtype=np.float32)
+        p = np.where(den > 0, e / np.where(den > 0, den, 1), 0).astype(np.float32)
+        o = p @ v[kv]
+        if token_mask is not None:
+            o *= np.asarray(token_mask[b], dtype=np.float32)[qs][:, None]
+        out[oi] = o
+    return out
+
+
+def sparse_prefill(q, k, v, *, scaling, sink, window, vertical, vertical_sqrt=0.0, n_route=64,
+                   pool="mean", queries="last", exact_tail=0, vertical_scope=0, scope_chunk=4096,
+                   dtype="bf16", rows=None, heads=None, idx=None, qpos=None):
+    """``RDAttention.sparse_prefill`` (``modal_rd/attention.py:176-206``) on post-RoPE inputs.
+
+    q [H, n, d], k/v [Hk, n, d]. Returns ``(out [len(heads), len(rows), d] fp32, idx [H, budget])``.
+    ``idx`` may be given to reuse routes already computed."""
+    H, n, d = np.shape(q)
+    hk = np.shape(k)[0]
+    g = H // hk
+    if idx is None:
+        idx = routes(q, k, scaling=scaling, sink=sink, window=window, vertical=vertical,
+                     vertical_sqrt=vertical_sqrt, n_route=n_route, pool=pool, queries=queries,
+                     dtype=dtype, qpos=qpos)
+    if vertical_scope:
+        chunk = scope_chunk
+        groups = -(-n // chunk)
+        starts = np.arange(groups) * chunk
+        active = (starts + chunk > n - vertical_scope)[None, :, None]
+        routed = np.where(active, idx[:, None, :], -1)
+    else:
+        chunk, routed = None, idx[:, None, :]
+    rows = np.arange(n) if rows is None else np.asarray(rows, dtype=np.int64)
+    heads = np.arange(H) if heads is None else np.asarray(heads, dtype=np.int64)
+    out = flash(q, k, v, routed, front=sink, window=window, num_heads=H, route_chunk=chunk,
+                kv_groups=g, scale=scaling, rows=rows, heads=heads)
+    r = min(exact_tail, n)
+    if r:
+        tail_rows = rows >= n - r
+        if tail_rows.any():
+            none = -np.ones((H, 1, 1), dtype=np.int32)
+            tail = flash(np.asarray(q)[:, n - r:], k, v, none, front=0, window=n, num_heads=H,
+                         kv_groups=g, scale=scaling, rows=rows[tail_rows] - (n - r), heads=heads)
+            out[:, tail_rows] = tail
+    return out, idx
