@@ -1,0 +1,421 @@
+#!/usr/bin/env python
+"""Benchmark of one Bigger Bird v3 sparse-prefill attention layer on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config config2] [--impl ours|reference]
+
+A step is one sparse-prefill layer: in-place RoPE on Q/K, routing (last 64 queries score every
+key, top-512 per query head), the sink + window + routed main pass, and the exact causal tail,
+all through the one-call C entry point ``bb_sparse_prefill``. The default workload is BASELINE
+config 2 (n = 131072, bf16, 32 Q / 8 KV heads, d = 128, sink 64, window 16384, vertical 512,
+tail 256). ``value`` is effective TFLOP/s: algorithmic FLOPs (4 * d * attended query-key pairs,
+counted exactly from the step's routes) over the max-over-ranks device time. With N > 1 the layer's
+KV heads are split across ranks (rank p owns KV heads [p*8/N, (p+1)*8/N) and their query heads);
+the single-layer path has no cross-rank data exchange, so the timing reductions are the only
+collectives.
+
+``--impl reference`` times the reference algorithm's CPU path (the numpy restatement under
+``oracle/``; the reference itself is Python and does not travel) on the host cores over a bounded
+sample of the same workload, and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from utmist_bigger_bird_b200.workload import CONFIGS, make_layer  # noqa: E402
+
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+TRAFFIC_FILE = ROOT / "profiles" / "flash_main_config2.md"
+
+
+def peaks():
+    if PEAKS_FILE.exists():
+        return json.loads(PEAKS_FILE.read_text()), "measured"
+    return FALLBACK, "fallback"
+
+
+def measured_traffic():
+    """Per-launch DRAM bytes of the main attention kernel from the committed ncu summary."""
+    if not TRAFFIC_FILE.exists():
+        return None
+    for line in TRAFFIC_FILE.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ----------------------------------------------------------------------------- FLOP counting
+
+def attended_pairs(n, sink, window, exact_tail, idx):
+    """Query-key pairs the layer attends (BASELINE section 2 formula), per query head, exact:
+    sink and window keys of the main rows, routed keys beyond each query's window, and the dense
+    causal tail rows. ``idx`` [heads, budget] are the step's routes."""
+    r = min(exact_tail, n)
+    m = n - r
+    q = np.arange(m, dtype=np.int64)
+    sink_p = np.minimum(sink, q + 1).sum()
+    lo = np.maximum(sink, q - window + 1)
+    win_p = np.maximum(0, q - lo + 1).sum()
+    tail_p = (np.arange(m, n, dtype=np.int64) + 1).sum()
+    idx = np.asarray(idx, dtype=np.int64)
+    routed = np.where(idx >= sink, np.maximum(0, m - (idx + window)), 0).sum(axis=-1)
+    return (sink_p + win_p + tail_p) * idx.shape[0] + routed.sum(), (sink_p + win_p, routed, tail_p)
+
+
+def main_pass_pairs(n, sink, window, exact_tail, idx):
+    r = min(exact_tail, n)
+    m = n - r
+    q = np.arange(m, dtype=np.int64)
+    base = np.minimum(sink, q + 1).sum() + np.maximum(0, q - np.maximum(sink, q - window + 1) + 1).sum()
+    idx = np.asarray(idx, dtype=np.int64)
+    routed = np.where(idx >= sink, np.maximum(0, m - (idx + window)), 0).sum()
+    return base * idx.shape[0] + routed
+
+
+# ----------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.proc = None
+        self.path = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.gpu = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            self.gpu = str(device.index or 0)
+
+    def __enter__(self):
+        try:
+            import tempfile
+            self.path = tempfile.NamedTemporaryFile(prefix="bb_clocks_", suffix=".csv", delete=False).name
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                rows.append((float(parts[0]), float(parts[1]), float(parts[2]), parts[3:]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3][1:5]) if v.lower() == "active"})
+        loaded = [r for r in rows if r[2] > 200.0] or rows
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
+
+
+# ----------------------------------------------------------------------------- reference arm
+
+def cpu_sample(cfg, kv_head=0, heads=2, rows_per_head=48):
+    """One bounded CPU sample of the workload with the oracle port: the routes of one KV head
+    (all n keys) plus ``rows_per_head`` spread query rows (incl. tail rows) of ``heads`` query
+    heads. Returns (seconds, algorithmic FLOPs of the sample)."""
+    from oracle import bigbird_oracle as orc
+    q, k, v, cos, sin, _ = make_layer(cfg, kv_heads=[kv_head])
+    g = cfg.heads // cfg.kv_heads
+    f = lambda t: t.float().numpy()  # noqa: E731
+    c, s = f(cos[0]), f(sin[0])
+    n = cfg.n
+    rows = np.unique(np.concatenate([np.linspace(0, n - 1 - cfg.exact_tail, rows_per_head - 8).astype(np.int64),
+                                     np.arange(n - 8, n)]))
+    t0 = time.perf_counter()
+    qn = orc.rope(f(q[0]), c, s, "bf16")
+    kn = orc.rope(f(k[0]), c, s, "bf16")
+    idx = orc.routes(qn, kn, scaling=cfg.scaling, sink=cfg.sink, window=cfg.window, vertical=cfg.vertical,
+                     n_route=cfg.n_route, dtype="bf16")
+    orc.sparse_prefill(qn[:heads], kn, f(v[0]), scaling=cfg.scaling, sink=cfg.sink, window=cfg.window,
+                       vertical=cfg.vertical, exact_tail=cfg.exact_tail, dtype="bf16", rows=rows,
+                       heads=np.arange(heads), idx=idx[:heads])
+    dt = time.perf_counter() - t0
+    # FLOPs of the sample: routing (2 QK^T passes of g*r rows over n keys) + attended pairs of the rows
+    route_flops = 2 * 2 * g * cfg.n_route * n * cfg.head_dim
+    r = min(cfg.exact_tail, n)
+    pairs = 0
+    for h in range(heads):
+        for qp in rows:
+            if qp >= n - r:
+                pairs += qp + 1
+            else:
+                lo = max(cfg.sink, qp - cfg.window + 1)
+                pairs += min(cfg.sink, qp + 1) + max(0, qp - lo + 1)
+                pairs += int(((idx[h] >= cfg.sink) & (idx[h] <= qp - cfg.window)).sum())
+    return dt, 4.0 * cfg.head_dim * pairs + route_flops
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = CONFIGS[args.config]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    for _ in range(args.warmup):
+        cpu_sample(cfg, rows_per_head=16)
+    times, flops = [], 0.0
+    for i in range(args.steps):
+        dt, fl = cpu_sample(cfg, kv_head=i % cfg.kv_heads)
+        times.append(dt)
+        flops += fl
+    total = sum(times)
+    value = flops / total / 1e12
+    sample = (f"per step: routes of 1 KV head over all {cfg.n} keys + 48 query rows x 2 query heads of "
+              f"{cfg.name} (numpy oracle port, fp32 math on bf16 inputs)")
+    line = {"impl": "reference", "metric": "eff_tflops_sparse_prefill_layer", "value": value, "unit": "TFLOP/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": cfg.name, "n": cfg.n, "sample": "bounded CPU sample (see cpu_baseline)"},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- our arm
+
+def event_time(fn, reps, stream):
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(reps):
+        fn()
+    e.record(stream)
+    e.synchronize()
+    return s.elapsed_time(e) / reps
+
+
+def run_ours(args):
+    import torch.distributed as dist
+
+    from utmist_bigger_bird_b200 import _lib, _ops
+    from utmist_bigger_bird_b200.attention import route_query_positions, vertical_budget
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    cfg = CONFIGS[args.config]
+    if cfg.kv_heads % world:
+        raise SystemExit(f"{cfg.kv_heads} KV heads do not split over {world} ranks")
+    per = cfg.kv_heads // world
+    kv_heads = list(range(rank * per, (rank + 1) * per))
+    g = cfg.heads // cfg.kv_heads
+    H = per * g
+    n, d = cfg.n, cfg.head_dim
+    q_h, k_h, v_h, cos_h, sin_h, _ = make_layer(cfg, kv_heads=kv_heads)
+    q_h, k_h, v_h, cos_h, sin_h = (t.pin_memory() for t in (q_h, k_h, v_h, cos_h, sin_h))
+    q0, k0, v, cos, sin = (t.to(dev) for t in (q_h, k_h, v_h, cos_h, sin_h))
+    q, k = q0.clone(), k0.clone()
+    budget = min(vertical_budget(n, cfg.vertical, 0.0), max(0, n - cfg.sink - cfg.window))
+    qpos = route_query_positions(n, min(cfg.n_route, n), "last", cfg.sink, cfg.window, dev)
+    out = torch.empty((n, H, d), device=dev, dtype=q.dtype).permute(1, 0, 2)
+    idx = torch.empty((H, budget), device=dev, dtype=torch.int32)
+    stream = torch.cuda.current_stream(dev)
+    L = _lib.lib()
+
+    def step():
+        _ops.sparse_prefill_(q[0], k[0], v[0], qpos, out, idx, sink=cfg.sink, window=cfg.window, budget=budget,
+                             exact_tail=cfg.exact_tail, scaling=cfg.scaling, cos=cos[0], sin=sin[0])
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier()
+    launches0 = L.bb_kernel_launches()
+    with ClockSampler(dev) as clocks:
+        barrier()
+        ms = event_time(step, args.steps, stream)
+        barrier()
+    launches = L.bb_kernel_launches() - launches0
+    clock = clocks.summary()
+
+    # exact FLOPs of this rank's step from its routes (routes are input-determined: identical every step)
+    pairs, _ = attended_pairs(n, cfg.sink, cfg.window, cfg.exact_tail, idx.cpu().numpy())
+    flops = 4.0 * d * float(pairs)
+    t = torch.tensor([ms, flops], dtype=torch.float64, device=dev)
+    if world > 1:
+        tmax = t[:1].clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        fsum = t[1:].clone()
+        dist.all_reduce(fsum, op=dist.ReduceOp.SUM)
+        ms_max, flops_all = tmax.item(), fsum.item()
+    else:
+        ms_max, flops_all = ms, flops
+    value = flops_all / (ms_max * 1e-3) / 1e12
+
+    # ---- dominant kernel (main sparse pass) and routing, timed alone on this rank
+    qr, kr = q0.clone(), k0.clone()
+    _ops.rope_inplace_(qr, cos, sin)
+    _ops.rope_inplace_(kr, cos, sin)
+    r_tail = min(cfg.exact_tail, n)
+    routed = idx.view(H, 1, -1)
+    chunk = 1 << (n - 1).bit_length()
+
+    def main_pass():
+        _ops.flash_(qr[0], kr[0], v[0], routed, out, front=cfg.sink, window=cfg.window, num_heads=H,
+                    kv_groups=g, route_chunk=chunk, scale=cfg.scaling, row_begin=0, row_end=n - r_tail)
+
+    def routing():
+        _ops.routes_(qr[0], kr[0], qpos, sink=cfg.sink, window=cfg.window, budget=budget, scaling=cfg.scaling)
+
+    def tail():
+        none = idx.view(H, 1, -1)[:, :, :0]
+        _ops.flash_(qr[0][:, n - r_tail:], kr[0], v[0], none, out[:, n - r_tail:], front=0, window=n,
+                    num_heads=H, kv_groups=g, route_chunk=chunk, scale=cfg.scaling)
+
+    for fn in (main_pass, routing, tail):
+        fn()
+    torch.cuda.synchronize(dev)
+    reps = max(3, min(args.steps, 10))
+    main_ms = event_time(main_pass, reps, stream)
+    route_ms = event_time(routing, reps * 3, stream)
+    tail_ms = event_time(tail, reps, stream)
+    main_flops = 4.0 * d * float(main_pass_pairs(n, cfg.sink, cfg.window, cfg.exact_tail, idx.cpu().numpy()))
+    pk, pk_kind = peaks()
+    achieved = main_flops / (main_ms * 1e-3) / 1e12
+    traffic = measured_traffic()
+    route_bytes = per * n * d * 2 + H * min(cfg.n_route, n) * d * 2 + H * budget * 4
+    route_gbs = route_bytes / (route_ms * 1e-3) / 1e9
+
+    # ---- dense causal SDPA on the same inputs (the reference's comparator, attn_bench.py:47)
+    import torch.nn.functional as F
+    dense = lambda: F.scaled_dot_product_attention(qr, kr, v, is_causal=True, scale=cfg.scaling,  # noqa: E731
+                                                   enable_gqa=True)
+    dense()
+    torch.cuda.synchronize(dev)
+    dense_ms = event_time(dense, max(2, reps // 2), stream)
+
+    # ---- end to end through the C entry point with host buffers (H2D inputs, D2H output)
+    out_h = torch.empty((n, H, d), dtype=q.dtype).pin_memory()
+    qe, ke = torch.empty_like(q0), torch.empty_like(k0)
+
+    def e2e_step():
+        qe.copy_(q_h, non_blocking=True)
+        ke.copy_(k_h, non_blocking=True)
+        v.copy_(v_h, non_blocking=True)
+        cos.copy_(cos_h, non_blocking=True)
+        sin.copy_(sin_h, non_blocking=True)
+        _ops.sparse_prefill_(qe[0], ke[0], v[0], qpos, out, idx, sink=cfg.sink, window=cfg.window, budget=budget,
+                             exact_tail=cfg.exact_tail, scaling=cfg.scaling, cos=cos[0], sin=sin[0])
+        out_h.copy_(out.permute(1, 0, 2), non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e2e_ms = event_time(e2e_step, max(3, min(args.steps, 5)), stream)
+    h2d = sum(t.numel() * t.element_size() for t in (q_h, k_h, v_h, cos_h, sin_h))
+    d2h = out_h.numel() * out_h.element_size()
+    te = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = flops_all / (te.item() * 1e-3) / 1e12
+
+    # ---- CPU baseline (rank 0, N = 1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        dt, fl = cpu_sample(cfg)
+        cpu = {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": f"routes of KV head 0 over all {n} keys + 48 spread/tail query rows x 2 query heads, "
+                         f"numpy oracle port ({dt:.1f} s)"}
+
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": "eff_tflops_sparse_prefill_layer", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_max, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{cfg.name}: one sparse-prefill attention layer (RoPE + routes + main + exact tail)",
+                   "n": n, "q_heads": cfg.heads, "kv_heads": cfg.kv_heads, "head_dim": d, "sink": cfg.sink,
+                   "window": cfg.window, "vertical": cfg.vertical, "exact_tail": cfg.exact_tail,
+                   "n_route": cfg.n_route, "parallelism": f"kv-head shards x{world}",
+                   "l2": "inputs (%.2f GB per rank) exceed L2; no flush" % ((q.numel() + k.numel() + v.numel()) * 2 / 1e9),
+                   "flops_per_step": flops_all},
+        "roofline": {"bound": "tensor", "kernel": "flash main pass (sink+window+routed)", "achieved": achieved,
+                     "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
+                     "peak_kind": f"{pk_kind} bf16 burst", "traffic": traffic, "launch_ms": main_ms,
+                     "flops_per_launch": main_flops},
+        "routing": {"bound": "hbm", "ms": route_ms, "achieved_gbs": route_gbs, "peak_gbs": pk["hbm_gbs"],
+                    "frac": route_gbs / pk["hbm_gbs"], "algorithmic_bytes": route_bytes},
+        "exact_tail_ms": tail_ms,
+        "dense_sdpa": {"ms": dense_ms, "speedup_sparse_vs_dense": dense_ms / ms},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms": te.item(), "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": int(launches),
+        "clocks": clock,
+        "gpu": torch.cuda.get_device_name(dev),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--config", default="config2", choices=sorted(CONFIGS))
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = p.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,153 @@
+/*
+ * bb_b200.h -- C ABI of the B200 (sm_100a) Bigger Bird v3 sparse-prefill library (libbb_b200.so).
+ *
+ * Plain pointers, sizes and element strides only; every tensor argument is a device pointer
+ * (unless stated otherwise) and every launch goes on the caller's CUDA stream. No call blocks
+ * the host or allocates device memory: scratch space is passed in by the caller, sized by the
+ * matching *_workspace_size query. Calls return a bb_status; bb_last_error() gives the message
+ * of the last failing call on the calling host thread.
+ *
+ * Reference interfaces replaced (paths inside derkychen/utmist-bigger-bird):
+ *   bb_rope_inplace      modal_rd/attention.py:51-60      rope_inplace(x, cos, sin)
+ *   bb_routes            modal_rd/attention.py:143-174    RDAttention.routes(q, k)
+ *   bb_flash             kernels/bigger_bird_flash.py:99-138  bigger_bird_flash(q, k, v, indices, ...)
+ *   bb_sparse_prefill    modal_rd/attention.py:176-206    RDAttention.sparse_prefill(q, k, v)
+ *                        (+ the in-place RoPE of forward, modal_rd/attention.py:121, when cos/sin given)
+ */
+#ifndef BB_B200_H
+#define BB_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define BB_API __attribute__((visibility("default")))
+#else
+#define BB_API
+#endif
+
+typedef struct CUstream_st* bb_stream_t; /* == cudaStream_t; NULL = legacy default stream */
+
+typedef enum {
+  BB_OK = 0,
+  BB_ERR_ARG = 1,          /* bad scalar argument (front < 0, window < 1, ...)          -> ValueError */
+  BB_ERR_SHAPE = 2,        /* inconsistent shapes / heads / route groups                -> ValueError */
+  BB_ERR_DTYPE = 3,        /* unsupported element type                                  -> ValueError */
+  BB_ERR_STRIDE = 4,       /* innermost stride != 1 or misaligned base/stride           -> ValueError */
+  BB_ERR_WORKSPACE = 5,    /* workspace missing or smaller than *_workspace_size        -> ValueError */
+  BB_ERR_LAUNCH = 6,       /* CUDA launch / attribute error                             -> RuntimeError */
+  BB_ERR_UNSUPPORTED = 7,  /* valid input outside what this build implements            -> ValueError */
+  BB_ERR_DEVICE = 8        /* not an sm_100 device / driver entry point missing         -> RuntimeError */
+} bb_status;
+
+typedef enum { BB_F16 = 0, BB_BF16 = 1, BB_F32 = 2 } bb_dtype;
+typedef enum { BB_POOL_MEAN = 0, BB_POOL_MAX = 1 } bb_pool;
+
+/* Message of the last error on this host thread ("" if none). */
+BB_API const char* bb_last_error(void);
+/* Library ABI version (BB_ABI_VERSION). */
+BB_API int bb_abi_version(void);
+#define BB_ABI_VERSION 1
+/* Number of CUDA kernels this library has launched in this process (all threads, all devices).
+ * Instrumentation for benchmarks; no counterpart in the reference. */
+BB_API uint64_t bb_kernel_launches(void);
+
+/* ------------------------------------------------------------------------------------------
+ * RoPE, in place: x[b,h,t,:] <- x*cos[b,t,:] + rotate_half(x)*sin[b,t,:], every op rounded to
+ * the element type exactly as the torch expression of modal_rd/attention.py:59 (bit-identical).
+ * x: [B, H, T, D] with element strides (sxb, sxh, sxt, 1); cos/sin: [B, T, D] with (scb, sct, 1)
+ * (scb may be 0 to broadcast). dtype: BB_F16, BB_BF16 or BB_F32. D must be even.
+ */
+BB_API int bb_rope_inplace(void* x, int dtype, int64_t B, int64_t H, int64_t T, int64_t D,
+                    int64_t sxb, int64_t sxh, int64_t sxt,
+                    const void* cos, const void* sin, int64_t scb, int64_t sct,
+                    bb_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Routes (RDAttention.routes, modal_rd/attention.py:143-174).
+ * For each KV head the routing queries q[h, qpos[i], :] of its `groups` query heads score every
+ * key: s = round_to_dtype(q . k) * scaling (the bf16/fp16 matmul output of :164), causal mask
+ * key > qpos -> -inf, fp32 softmax over all keys, then the mean (or max) over the r routing
+ * queries gives col[h, key]. Columns [0, sink) and the Python slice [n - window:] are set to -1;
+ * the `budget` largest columns per query head are returned sorted ascending (int32). Ties at the
+ * budget-th score are broken towards lower key positions.
+ */
+typedef struct {
+  const void* q;  int64_t sq_h, sq_t;   /* [H, n, d], innermost stride 1 (post-RoPE queries) */
+  const void* k;  int64_t sk_h, sk_t;   /* [Hk, n, d], innermost stride 1 (post-RoPE keys)   */
+  const int64_t* qpos;                  /* [r] device positions of the routing queries       */
+  int64_t heads, kv_heads, n, d, r;
+  int64_t sink, window, budget;
+  float scaling;
+  int pool;                             /* bb_pool */
+  int dtype;                            /* BB_F16 or BB_BF16 */
+  int32_t* out_idx; int64_t so_h;       /* [H, budget] int32 */
+  float* out_col;                       /* optional [H, n] fp32 copy of the column scores (NULL: none) */
+} bb_routes_args;
+
+BB_API int bb_routes_workspace_size(const bb_routes_args* a, size_t* bytes);
+BB_API int bb_routes(const bb_routes_args* a, void* workspace, size_t workspace_bytes, bb_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Sparse flash attention (bigger_bird_flash, kernels/bigger_bird_flash.py:99-138).
+ * One online softmax per query over the union of: sink keys [0, front), the causal window
+ * [q - window + 1, q], and routed keys idx[bh, group(q), :] that lie in [front, q - window]
+ * (disjoint sets; -1 or out-of-range slots are empty). Query j of T sits at absolute position
+ * n - T + j. Query head h reads KV head (h / num_heads) * (num_heads / kv_groups)
+ * + (h % num_heads) / kv_groups. token_mask (optional, [B, n] bytes, B = BH / num_heads) drops
+ * masked keys and zeroes masked query rows. Fully masked rows give 0.
+ * Rows [row_begin, row_end) of T are computed and written; other output rows are untouched.
+ */
+typedef struct {
+  const void* q;  int64_t sq_h, sq_t;       /* [BH, T, D] */
+  const void* k;  int64_t sk_h, sk_t;       /* [BH/kv_groups, n, D] */
+  const void* v;  int64_t sv_h, sv_t;       /* [BH/kv_groups, n, D] */
+  const int32_t* idx; int64_t si_h, si_g, si_k; /* [BH, G, K] int32 (K may be 0) */
+  const uint8_t* token_mask; int64_t sm_b, sm_t; /* [B, n] or NULL */
+  void* out; int64_t so_h, so_t;            /* [BH, T, D] */
+  int64_t bh, t, n, d;
+  int64_t num_heads, kv_groups;
+  int64_t front, window;
+  int64_t route_k, route_groups, route_chunk;
+  int64_t row_begin, row_end;
+  float scale;
+  int dtype;                                /* BB_F16 or BB_BF16 */
+} bb_flash_args;
+
+BB_API int bb_flash_workspace_size(const bb_flash_args* a, size_t* bytes);
+BB_API int bb_flash(const bb_flash_args* a, void* workspace, size_t workspace_bytes, bb_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Whole sparse prefill of one layer (RDAttention.sparse_prefill, modal_rd/attention.py:176-206):
+ * [RoPE in place on q and k when cos/sin are given] -> routes -> main sparse pass over rows
+ * [0, n - exact_tail) -> exact causal tail over the last exact_tail rows (front=0, window=n).
+ * q: [H, n, d]; k, v: [Hk, n, d]; out: [H, n, d]. vertical_scope/scope_chunk as in :187-194.
+ * out_idx receives the routes [H, budget] (RDAttention.last_routes).
+ */
+typedef struct {
+  void* q;  int64_t sq_h, sq_t;
+  void* k;  int64_t sk_h, sk_t;
+  const void* v;  int64_t sv_h, sv_t;
+  const void* cos; const void* sin; int64_t sc_t;   /* [n, d] or NULL (no RoPE) */
+  const int64_t* qpos;                            /* [r] routing query positions (device) */
+  void* out; int64_t so_h, so_t;
+  int32_t* out_idx; int64_t si_h;
+  int64_t heads, kv_heads, n, d, r;
+  int64_t sink, window, budget, exact_tail, vertical_scope, scope_chunk;
+  float scaling;
+  int pool;
+  int dtype;
+} bb_prefill_args;
+
+BB_API int bb_sparse_prefill_workspace_size(const bb_prefill_args* a, size_t* bytes);
+BB_API int bb_sparse_prefill(const bb_prefill_args* a, void* workspace, size_t workspace_bytes,
+                      bb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BB_B200_H */

@@ -1,1 +1,12 @@
-"""B200-native (sm_100a) Bigger Bird v3 sparse prefill attention."""
+"""B200-native (sm_100a) Bigger Bird v3 sparse prefill attention.
+
+Drop-in surfaces of the reference project (derkychen/utmist-bigger-bird):
+  * ``bigger_bird_flash``   -- kernels/bigger_bird_flash.py
+  * ``RDAttention``, ``install``, ``rope_inplace``, ``vertical_budget`` -- modal_rd/attention.py
+The compute runs in ``libbb_b200.so`` (C ABI: include/bb_b200.h); build it with
+``python -m utmist_bigger_bird_b200.build``.
+"""
+from .attention import RDAttention, forward_pool, install, rope_inplace, vertical_budget  # noqa: F401
+from .bigger_bird_flash import bigger_bird_flash  # noqa: F401
+
+__all__ = ["RDAttention", "install", "rope_inplace", "vertical_budget", "forward_pool", "bigger_bird_flash"]

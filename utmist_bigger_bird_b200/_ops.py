@@ -1,0 +1,140 @@
+"""torch-tensor wrappers over the C ABI (device pointers, element strides, current stream).
+
+Every function launches on ``torch.cuda.current_stream()`` and returns without synchronising.
+Scratch memory comes from torch's caching allocator and is passed to the library explicitly.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float16: _lib.BB_F16, torch.bfloat16: _lib.BB_BF16, torch.float32: _lib.BB_F32}
+
+
+def _stream(t: torch.Tensor):
+    return C.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _rows_ok(t: torch.Tensor) -> bool:
+    """Innermost stride 1 and every row on a 16-byte boundary (the kernels' load granularity)."""
+    es = t.element_size()
+    return (t.stride(-1) == 1 or t.shape[-1] == 1) and t.data_ptr() % 16 == 0 and all(
+        (s * es) % 16 == 0 for s in t.stride()[:-1])
+
+
+def rows_view(t: torch.Tensor) -> torch.Tensor:
+    """``t`` itself when the kernels can read it in place, else a contiguous copy."""
+    return t if _rows_ok(t) else t.contiguous()
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor | None:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device) if nbytes else None
+
+
+def rope_inplace_(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """x [B, H, T, D] (any strides with innermost 1), cos/sin [B or 1, T, D] -> x rotated in place."""
+    if not x.is_cuda:
+        raise ValueError("rope_inplace requires CUDA tensors")
+    if x.dtype not in _DT or cos.dtype != x.dtype or sin.dtype != x.dtype:
+        raise ValueError("rope_inplace: x, cos and sin must share one of f16/bf16/f32")
+    if x.ndim != 4 or cos.ndim != 3 or cos.shape != sin.shape or cos.stride() != sin.stride():
+        raise ValueError("rope_inplace: x [B,H,T,D] and cos/sin [B,T,D] expected")
+    B, H, T, D = x.shape
+    if cos.shape[-2:] != (T, D) or cos.shape[0] not in (1, B):
+        raise ValueError("rope_inplace: cos/sin do not match x")
+    if x.stride(-1) != 1 or cos.stride(-1) != 1:
+        raise ValueError("rope_inplace: innermost stride must be 1")
+    scb = 0 if cos.shape[0] == 1 else cos.stride(0)
+    _lib.check(_lib.lib().bb_rope_inplace(_ptr(x), _DT[x.dtype], B, H, T, D, x.stride(0), x.stride(1),
+                                          x.stride(2), _ptr(cos), _ptr(sin), scb, cos.stride(1),
+                                          _stream(x)), "rope_inplace")
+    return x
+
+
+def routes_(q: torch.Tensor, k: torch.Tensor, qpos: torch.Tensor, *, sink: int, window: int,
+            budget: int, scaling: float, pool: str = "mean", out_col: torch.Tensor | None = None):
+    """q [H, n, d], k [Hk, n, d] (post-RoPE), qpos [r] int64 -> int32 [H, budget] sorted."""
+    if q.dtype not in (torch.float16, torch.bfloat16) or k.dtype != q.dtype:
+        raise ValueError("routes requires CUDA FP16/BF16 q and k")
+    q, k = rows_view(q), rows_view(k)
+    qpos = qpos.to(device=q.device, dtype=torch.int64).contiguous()
+    H, n, d = q.shape
+    out = torch.empty((H, budget), dtype=torch.int32, device=q.device)
+    a = _lib.RoutesArgs(q=q.data_ptr(), sq_h=q.stride(0), sq_t=q.stride(1),
+                        k=k.data_ptr(), sk_h=k.stride(0), sk_t=k.stride(1), qpos=qpos.data_ptr(),
+                        heads=H, kv_heads=k.shape[0], n=n, d=d, r=qpos.numel(), sink=sink,
+                        window=window, budget=budget, scaling=scaling,
+                        pool=_lib.BB_POOL_MAX if pool == "max" else _lib.BB_POOL_MEAN,
+                        dtype=_DT[q.dtype], out_idx=out.data_ptr(), so_h=max(budget, 1),
+                        out_col=out_col.data_ptr() if out_col is not None else None)
+    L = _lib.lib()
+    nbytes = C.c_size_t(0)
+    _lib.check(L.bb_routes_workspace_size(C.byref(a), C.byref(nbytes)), "routes")
+    ws = _workspace(nbytes.value, q.device)
+    _lib.check(L.bb_routes(C.byref(a), _ptr(ws), nbytes.value, _stream(q)), "routes")
+    return out
+
+
+def flash_(q, k, v, idx, out, *, front, window, num_heads, kv_groups, route_chunk, scale,
+           token_mask=None, row_begin=0, row_end=None):
+    """Launch the sparse flash kernel. q [BH,T,D], k/v [BH/g,N,D], idx [BH,G,K] int32,
+    out [BH,T,D] (written on rows [row_begin, row_end))."""
+    bh, t, d = q.shape
+    row_end = t if row_end is None else row_end
+    q, k, v = rows_view(q), rows_view(k), rows_view(v)
+    if out.stride(-1) != 1:
+        raise ValueError("out must have innermost stride 1")
+    G, K = idx.shape[1], idx.shape[2]
+    a = _lib.FlashArgs(q=q.data_ptr(), sq_h=q.stride(0), sq_t=q.stride(1),
+                       k=k.data_ptr(), sk_h=k.stride(0), sk_t=k.stride(1),
+                       v=v.data_ptr(), sv_h=v.stride(0), sv_t=v.stride(1),
+                       idx=idx.data_ptr() if idx.numel() else None,
+                       si_h=idx.stride(0), si_g=idx.stride(1), si_k=idx.stride(2),
+                       token_mask=token_mask.data_ptr() if token_mask is not None else None,
+                       sm_b=token_mask.stride(0) if token_mask is not None else 0,
+                       sm_t=token_mask.stride(1) if token_mask is not None else 0,
+                       out=out.data_ptr(), so_h=out.stride(0), so_t=out.stride(1),
+                       bh=bh, t=t, n=k.shape[1], d=d, num_heads=num_heads, kv_groups=kv_groups,
+                       front=front, window=window, route_k=K, route_groups=G, route_chunk=route_chunk,
+                       row_begin=row_begin, row_end=row_end, scale=scale, dtype=_DT[q.dtype])
+    L = _lib.lib()
+    nbytes = C.c_size_t(0)
+    _lib.check(L.bb_flash_workspace_size(C.byref(a), C.byref(nbytes)), "bigger_bird_flash")
+    ws = _workspace(nbytes.value, q.device)
+    _lib.check(L.bb_flash(C.byref(a), _ptr(ws), nbytes.value, _stream(q)), "bigger_bird_flash")
+    return out
+
+
+def sparse_prefill_(q, k, v, qpos, out, out_idx, *, sink, window, budget, exact_tail, scaling,
+                    pool="mean", vertical_scope=0, scope_chunk=4096, cos=None, sin=None):
+    """One C call for the whole layer: [RoPE] + routes + main pass + exact tail.
+    q [H,n,d], k/v [Hk,n,d], out [H,n,d], out_idx [H,budget] int32, cos/sin [n,d] or None."""
+    H, n, d = q.shape
+    if cos is not None and (cos.stride(-1) != 1 or sin.stride() != cos.stride()):
+        raise ValueError("cos/sin must share strides with innermost stride 1")
+    qpos = qpos.to(device=q.device, dtype=torch.int64).contiguous()
+    a = _lib.PrefillArgs(q=q.data_ptr(), sq_h=q.stride(0), sq_t=q.stride(1),
+                         k=k.data_ptr(), sk_h=k.stride(0), sk_t=k.stride(1),
+                         v=v.data_ptr(), sv_h=v.stride(0), sv_t=v.stride(1),
+                         cos=cos.data_ptr() if cos is not None else None,
+                         sin=sin.data_ptr() if sin is not None else None,
+                         sc_t=cos.stride(0) if cos is not None else 0,
+                         qpos=qpos.data_ptr(), out=out.data_ptr(), so_h=out.stride(0), so_t=out.stride(1),
+                         out_idx=out_idx.data_ptr(), si_h=max(budget, 1),
+                         heads=H, kv_heads=k.shape[0], n=n, d=d, r=qpos.numel(), sink=sink,
+                         window=window, budget=budget, exact_tail=exact_tail,
+                         vertical_scope=vertical_scope, scope_chunk=scope_chunk, scaling=scaling,
+                         pool=_lib.BB_POOL_MAX if pool == "max" else _lib.BB_POOL_MEAN, dtype=_DT[q.dtype])
+    L = _lib.lib()
+    nbytes = C.c_size_t(0)
+    _lib.check(L.bb_sparse_prefill_workspace_size(C.byref(a), C.byref(nbytes)), "sparse_prefill")
+    ws = _workspace(nbytes.value, q.device)
+    _lib.check(L.bb_sparse_prefill(C.byref(a), _ptr(ws), nbytes.value, _stream(q)), "sparse_prefill")
+    return out

@@ -1,0 +1,96 @@
+// In-place RoPE, bit-identical to rope_inplace (modal_rd/attention.py:51-60), i.e. to the torch
+// expression `x * cos + rotate_half(x) * sin` where every op rounds to the tensor's dtype.
+// HBM-bound elementwise work: each thread rotates VEC (i, i + D/2) pairs of one row, reading
+// and writing x once and cos/sin once.
+#include "bb_common.cuh"
+
+namespace bb {
+namespace {
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) rope_kernel(T* __restrict__ x, const T* __restrict__ cos,
+                                                   const T* __restrict__ sin, int64_t B, int64_t H,
+                                                   int64_t T_, int64_t D, int64_t sxb, int64_t sxh,
+                                                   int64_t sxt, int64_t scb, int64_t sct) {
+  using E = Elem<T>;
+  const int64_t half = D / 2;
+  const int64_t chunks = half / VEC;
+  const int64_t total = B * H * T_ * chunks;
+  for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < total;
+       w += (int64_t)gridDim.x * blockDim.x) {
+    int64_t c = w % chunks;
+    int64_t r = w / chunks;
+    const int64_t t = r % T_;
+    r /= T_;
+    const int64_t h = r % H;
+    const int64_t b = r / H;
+    T* row = x + b * sxb + h * sxh + t * sxt;
+    const T* cr = cos + b * scb + t * sct;
+    const T* sr = sin + b * scb + t * sct;
+    const int64_t i0 = c * VEC;
+    T x1[VEC], x2[VEC], c1[VEC], c2[VEC], s1[VEC], s2[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      x1[j] = row[i0 + j];
+      x2[j] = row[i0 + half + j];
+      c1[j] = cr[i0 + j];
+      c2[j] = cr[i0 + half + j];
+      s1[j] = sr[i0 + j];
+      s2[j] = sr[i0 + half + j];
+    }
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const float a = E::to_f(x1[j]), bq = E::to_f(x2[j]);
+      // first half:  x1*cos + (-x2)*sin ; second half: x2*cos + x1*sin
+      const float lo = E::round(__fadd_rn(E::round(__fmul_rn(a, E::to_f(c1[j]))),
+                                          E::round(__fmul_rn(-bq, E::to_f(s1[j])))));
+      const float hi = E::round(__fadd_rn(E::round(__fmul_rn(bq, E::to_f(c2[j]))),
+                                          E::round(__fmul_rn(a, E::to_f(s2[j])))));
+      row[i0 + j] = E::from_f(lo);
+      row[i0 + half + j] = E::from_f(hi);
+    }
+  }
+}
+
+template <typename T>
+int launch_rope(void* x, int64_t B, int64_t H, int64_t T_, int64_t D, int64_t sxb, int64_t sxh,
+                int64_t sxt, const void* cos, const void* sin, int64_t scb, int64_t sct,
+                cudaStream_t stream) {
+  const int64_t half = D / 2;
+  const int vec = (half % 8 == 0) ? 8 : ((half % 4 == 0) ? 4 : 1);
+  const int64_t total = B * H * T_ * (half / vec);
+  if (total == 0) return BB_OK;
+  const int64_t grid = std::min<int64_t>(cdiv(total, 256), (int64_t)num_sms() * 16);
+  T* xp = static_cast<T*>(x);
+  const T* cp = static_cast<const T*>(cos);
+  const T* sp = static_cast<const T*>(sin);
+  if (vec == 8)
+    rope_kernel<T, 8><<<grid, 256, 0, stream>>>(xp, cp, sp, B, H, T_, D, sxb, sxh, sxt, scb, sct);
+  else if (vec == 4)
+    rope_kernel<T, 4><<<grid, 256, 0, stream>>>(xp, cp, sp, B, H, T_, D, sxb, sxh, sxt, scb, sct);
+  else
+    rope_kernel<T, 1><<<grid, 256, 0, stream>>>(xp, cp, sp, B, H, T_, D, sxb, sxh, sxt, scb, sct);
+  BB_CHECK_LAUNCH("rope_kernel");
+  return BB_OK;
+}
+
+}  // namespace
+
+int rope_inplace(void* x, int dtype, int64_t B, int64_t H, int64_t T_, int64_t D, int64_t sxb,
+                 int64_t sxh, int64_t sxt, const void* cos, const void* sin, int64_t scb,
+                 int64_t sct, cudaStream_t stream) {
+  if (!x || !cos || !sin) return fail(BB_ERR_ARG, "rope: null pointer");
+  if (B < 0 || H < 0 || T_ < 0 || D <= 0 || (D & 1)) return fail(BB_ERR_SHAPE, "rope: bad shape (D must be even)");
+  switch (dtype) {
+    case BB_BF16:
+      return launch_rope<__nv_bfloat16>(x, B, H, T_, D, sxb, sxh, sxt, cos, sin, scb, sct, stream);
+    case BB_F16:
+      return launch_rope<__half>(x, B, H, T_, D, sxb, sxh, sxt, cos, sin, scb, sct, stream);
+    case BB_F32:
+      return launch_rope<float>(x, B, H, T_, D, sxb, sxh, sxt, cos, sin, scb, sct, stream);
+    default:
+      return fail(BB_ERR_DTYPE, "rope: dtype must be f16, bf16 or f32");
+  }
+}
+
+}  // namespace bb
