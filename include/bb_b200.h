@@ -92,6 +92,25 @@ typedef struct {
 BB_API int bb_routes_workspace_size(const bb_routes_args* a, size_t* bytes);
 BB_API int bb_routes(const bb_routes_args* a, void* workspace, size_t workspace_bytes, bb_stream_t stream);
 
+/* bb_routes for callers that cannot allocate device memory. This entry point has no
+ * counterpart in the reference. Some host programs reserve the whole GPU for their own memory
+ * pool. A serving engine that pre-sizes its KV cache is one example. Some FFI callers have no
+ * device allocator at all. Neither can hand this library a fresh workspace. This call computes
+ * exactly what bb_routes computes (same kernels, same results). Its scratch lives in one fixed
+ * array inside the library, BB_ROUTES_NOALLOC_SCRATCH_BYTES (24 MiB) per GPU. Every GPU that
+ * loads the library holds that array until the process exits. It is enough for the 128K-token,
+ * 32-query-head layer (about 19 MB). A request needing more is rejected with BB_ERR_WORKSPACE
+ * and a message giving both sizes, before anything is launched. The caller still passes q, k,
+ * qpos and the outputs.
+ * The first call on each device looks up the array's device address, with that device current.
+ * Make that first call before any stream capture. All calls share the one array, and it keeps
+ * the previous call's contents. That is harmless here: every scratch byte a call reads is
+ * written earlier in the same call. Calls that overlap on the GPU race on the array, for
+ * example on two streams of one device. Serialize them. The call never runs cudaMalloc,
+ * cudaFree or any allocating library routine. */
+#define BB_ROUTES_NOALLOC_SCRATCH_BYTES ((size_t)24 << 20)
+BB_API int bb_routes_noalloc(const bb_routes_args* a, bb_stream_t stream);
+
 /* ------------------------------------------------------------------------------------------
  * Sparse flash attention (bigger_bird_flash, kernels/bigger_bird_flash.py:99-138).
  * One online softmax per query over the union of: sink keys [0, front), the causal window

@@ -68,6 +68,7 @@ EXPORTS = {
     "bb_rope_inplace": (C.c_int, [vp, C.c_int, i64, i64, i64, i64, i64, i64, i64, vp, vp, i64, i64, vp]),
     "bb_routes_workspace_size": (C.c_int, [C.POINTER(RoutesArgs), C.POINTER(C.c_size_t)]),
     "bb_routes": (C.c_int, [C.POINTER(RoutesArgs), vp, C.c_size_t, vp]),
+    "bb_routes_noalloc": (C.c_int, [C.POINTER(RoutesArgs), vp]),
     "bb_flash_workspace_size": (C.c_int, [C.POINTER(FlashArgs), C.POINTER(C.c_size_t)]),
     "bb_flash": (C.c_int, [C.POINTER(FlashArgs), vp, C.c_size_t, vp]),
     "bb_sparse_prefill_workspace_size": (C.c_int, [C.POINTER(PrefillArgs), C.POINTER(C.c_size_t)]),

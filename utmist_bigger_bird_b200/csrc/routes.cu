@@ -13,6 +13,7 @@
 // of 16, so every 16-row MMA tile belongs to exactly one query head and pooling is a fixed-order
 // reduction (deterministic run to run).
 #include <algorithm>
+#include <mutex>
 
 #include "bb_common.cuh"
 
@@ -522,3 +523,59 @@ int routes(const bb_routes_args* a, void* ws, size_t ws_bytes, cudaStream_t stre
 }
 
 }  // namespace bb
+
+// ---------------------------------------------------------------------------------------------
+// bb_routes_noalloc: routing with its scratch in a fixed device array instead of a caller
+// workspace, for hosts that cannot hand out device memory (a program that has reserved the GPU
+// for its own pool, or an FFI caller without a device allocator). The array is allocated when
+// the library's module is loaded on a device and is held by that device until the process
+// exits; nothing here calls cudaMalloc, cudaFree or an allocating library routine.
+//
+// Host code must not pass `g_routes_scratch` itself to a kernel: in host code the name is a
+// host-side stand-in, not a device address. The device address is looked up once per device
+// with cudaGetSymbolAddress, with that device current, on the first call made on it.
+static __device__ __align__(256) unsigned char g_routes_scratch[BB_ROUTES_NOALLOC_SCRATCH_BYTES];
+
+namespace bb {
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+int routes_scratch_address(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(BB_ERR_DEVICE, "routes_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(BB_ERR_DEVICE, "routes_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_routes_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(BB_ERR_DEVICE, "routes_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return BB_OK;
+}
+
+}  // namespace
+}  // namespace bb
+
+extern "C" int bb_routes_noalloc(const bb_routes_args* a, bb_stream_t stream) {
+  size_t need = 0;
+  int st = bb::routes_workspace_size(a, &need);
+  if (st) return st;
+  if (need > BB_ROUTES_NOALLOC_SCRATCH_BYTES)
+    return bb::fail(BB_ERR_WORKSPACE,
+                    "routes_noalloc: this request needs %zu bytes of scratch, more than the library's "
+                    "fixed %zu; use bb_routes with a caller workspace",
+                    need, (size_t)BB_ROUTES_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  st = bb::routes_scratch_address(&scratch);
+  if (st) return st;
+  // Every scratch byte the routing kernels read is written earlier in the same call (row
+  // statistics, merged statistics, column scores), so the previous call's contents need no clearing.
+  return bb::routes(a, scratch, BB_ROUTES_NOALLOC_SCRATCH_BYTES, bb::as_stream(stream));
+}
