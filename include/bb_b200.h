@@ -55,6 +55,11 @@ BB_API int bb_abi_version(void);
 /* Number of CUDA kernels this library has launched in this process (all threads, all devices).
  * Instrumentation for benchmarks; no counterpart in the reference. */
 BB_API uint64_t bb_kernel_launches(void);
+/* Reads and clears the current device's fault word. Kernels bound every wait on another warp's
+ * progress (about 2 s); a kernel that gives up a wait records a non-zero code here, drains its
+ * copies, frees its tensor memory and returns instead of hanging. Synchronous (copies 4 bytes
+ * from the device). No counterpart in the reference. */
+BB_API int bb_device_fault(int* code);
 
 /* ------------------------------------------------------------------------------------------
  * RoPE, in place: x[b,h,t,:] <- x*cos[b,t,:] + rotate_half(x)*sin[b,t,:], every op rounded to

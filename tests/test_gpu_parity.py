@@ -338,3 +338,13 @@ def test_no_kv_sized_copies():
     copies = [(b, f) for b, f in log.records if b >= h_wide // 4 and any(
         c in f for c in ("repeat_interleave", "index_select", "clone", "contiguous", "_to_copy"))]
     assert not copies, copies
+
+
+def test_no_device_fault_recorded():
+    """No kernel gave up a bounded wait during the tests above (the fault word stays 0)."""
+    import ctypes as C
+    from utmist_bigger_bird_b200 import _lib
+    torch.cuda.synchronize()
+    code = C.c_int(-1)
+    _lib.check(_lib.lib().bb_device_fault(C.byref(code)), "device_fault")
+    assert code.value == 0, f"a kernel recorded fault code {code.value}"

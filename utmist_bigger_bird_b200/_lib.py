@@ -65,6 +65,7 @@ EXPORTS = {
     "bb_last_error": (C.c_char_p, []),
     "bb_abi_version": (C.c_int, []),
     "bb_kernel_launches": (C.c_uint64, []),
+    "bb_device_fault": (C.c_int, [C.POINTER(C.c_int)]),
     "bb_rope_inplace": (C.c_int, [vp, C.c_int, i64, i64, i64, i64, i64, i64, i64, vp, vp, i64, i64, vp]),
     "bb_routes_workspace_size": (C.c_int, [C.POINTER(RoutesArgs), C.POINTER(C.c_size_t)]),
     "bb_routes": (C.c_int, [C.POINTER(RoutesArgs), vp, C.c_size_t, vp]),

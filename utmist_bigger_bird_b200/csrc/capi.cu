@@ -4,7 +4,7 @@
 #include <cstring>
 #include <string>
 
-#include "bb_common.cuh"
+#include "flash.cuh"
 
 namespace bb {
 
@@ -152,6 +152,11 @@ const char* bb_last_error(void) { return bb::g_last_error.c_str(); }
 int bb_abi_version(void) { return BB_ABI_VERSION; }
 
 uint64_t bb_kernel_launches(void) { return bb::g_launches.load(std::memory_order_relaxed); }
+
+int bb_device_fault(int* code) {
+  if (!code) return bb::fail(BB_ERR_ARG, "device_fault: null pointer");
+  return bb::device_fault_take(code);
+}
 
 int bb_rope_inplace(void* x, int dtype, int64_t B, int64_t H, int64_t T, int64_t D, int64_t sxb,
                     int64_t sxh, int64_t sxt, const void* cos, const void* sin, int64_t scb,

@@ -1,0 +1,35 @@
+// Parameters shared by the two sparse-attention kernels (flash_mma.cu: mma.sync for head_dim < 128;
+// flash_tc.cu: tcgen05/TMEM/TMA for head_dim 128).
+#pragma once
+
+#include "bb_common.cuh"
+
+namespace bb {
+
+constexpr float LOG2E = 1.4426950408889634f;
+
+struct FlashParams {
+  const void* q; int64_t sq_h, sq_t;
+  const void* k; int64_t sk_h, sk_t;
+  const void* v; int64_t sv_h, sv_t;
+  const int32_t* idx; int64_t si_h, si_g, si_k;
+  const uint8_t* mask; int64_t sm_b, sm_t;
+  void* out; int64_t so_h, so_t;
+  int64_t t, n, d, offset;
+  int64_t num_heads, kv_groups;
+  int64_t front, window;       // front already clipped to n
+  int64_t route_k, route_groups, route_chunk;
+  int64_t row_begin, row_end;
+  float scale_log2;
+  int splits;
+  float* part_acc;             // [splits][BH][T][128] (split mode)
+  float2* part_ml;             // [splits][BH][T]: (running max in log2 units, sum)
+  int64_t bh;
+};
+
+int flash_tc_launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream);
+int flash_tc_splits(const bb_flash_args* a, int sms);
+// Reads and clears the current device's fault word (set by a kernel whose bounded wait gave up).
+int device_fault_take(int* code);
+
+}  // namespace bb

@@ -14,33 +14,14 @@
 // flash_combine_kernel.
 #include <algorithm>
 
-#include "bb_common.cuh"
+#include "flash.cuh"
 
 namespace bb {
 
 constexpr int FM_BM = 64;
 constexpr int FM_BN = 64;
 constexpr int FM_THREADS = 128;
-constexpr float LOG2E = 1.4426950408889634f;
 
-struct FlashParams {
-  const void* q; int64_t sq_h, sq_t;
-  const void* k; int64_t sk_h, sk_t;
-  const void* v; int64_t sv_h, sv_t;
-  const int32_t* idx; int64_t si_h, si_g, si_k;
-  const uint8_t* mask; int64_t sm_b, sm_t;
-  void* out; int64_t so_h, so_t;
-  int64_t t, n, d, offset;
-  int64_t num_heads, kv_groups;
-  int64_t front, window;       // front already clipped to n
-  int64_t route_k, route_groups, route_chunk;
-  int64_t row_begin, row_end;
-  float scale_log2;
-  int splits;
-  float* part_acc;             // [splits][BH][T][D] (split mode)
-  float2* part_ml;             // [splits][BH][T]
-  int64_t bh;
-};
 
 namespace {
 
@@ -406,13 +387,21 @@ int flash_check_pointers(const bb_flash_args* a) {
   if (!al(a->q) || !al(a->k) || !al(a->v) || (a->sq_h * 2) % 16 || (a->sq_t * 2) % 16 ||
       (a->sk_h * 2) % 16 || (a->sk_t * 2) % 16 || (a->sv_h * 2) % 16 || (a->sv_t * 2) % 16)
     return fail(BB_ERR_STRIDE, "flash: q/k/v rows must start on 16-byte boundaries");
+  if (a->d == 128 && (!al(a->out) || (a->so_h * 2) % 16 || (a->so_t * 2) % 16))
+    return fail(BB_ERR_STRIDE, "flash: output rows must start on 16-byte boundaries");
   return BB_OK;
 }
+
+// head_dim 128 (every Llama-shaped layer) runs on the tcgen05/TMEM kernel; smaller head dims
+// (the reference's unit-test shapes) run on the mma.sync kernel.
+bool use_tc(const bb_flash_args* a) { return a->d == 128; }
+
+int splits_of(const bb_flash_args* a) { return use_tc(a) ? flash_tc_splits(a, num_sms()) : choose_splits(a); }
 
 int flash_workspace_size(const bb_flash_args* a, size_t* bytes) {
   int st = flash_check(a);
   if (st) return st;
-  const int splits = choose_splits(a);
+  const int splits = splits_of(a);
   *bytes = splits > 1 ? align_up((size_t)splits * a->bh * a->t * dpad_of(a->d) * 4, 256) +
                             align_up((size_t)splits * a->bh * a->t * 8, 256)
                       : 0;
@@ -441,12 +430,13 @@ int flash(const bb_flash_args* a, void* ws, size_t ws_bytes, cudaStream_t stream
   p.route_k = a->route_k; p.route_groups = a->route_groups; p.route_chunk = a->route_chunk;
   p.row_begin = a->row_begin; p.row_end = a->row_end;
   p.scale_log2 = a->scale * LOG2E;
-  p.splits = choose_splits(a);
+  p.splits = splits_of(a);
   p.bh = a->bh;
   const int dp = dpad_of(a->d);
   char* w = static_cast<char*>(ws);
   p.part_acc = reinterpret_cast<float*>(w);
   p.part_ml = reinterpret_cast<float2*>(w + (p.splits > 1 ? align_up((size_t)p.splits * a->bh * a->t * dp * 4, 256) : 0));
+  if (use_tc(a)) return flash_tc_launch(a, p, stream);
   if (a->dtype == BB_BF16) {
     if (dp == 32) return launch_flash_t<__nv_bfloat16, 32>(a, p, stream);
     if (dp == 64) return launch_flash_t<__nv_bfloat16, 64>(a, p, stream);

@@ -1,0 +1,717 @@
+// Sparse flash attention for head_dim 128 on B200: tcgen05 MMA with TMEM accumulators, TMA tile
+// loads, warp-specialised.
+//
+// Semantics are those of bigger_bird_flash (kernels/bigger_bird_flash.py:42-96): one online
+// softmax per query over the disjoint union of the sink keys [0, front), the causal window
+// [q-W+1, q] and the routed keys idx[h, group(q), :] in [front, q-W]; scores q.k*scale*log2(e),
+// exp2, P rounded to the input dtype before P.V, output acc / max(l, 1e-20), fully masked rows 0.
+//
+// One CTA computes a 128-query tile of one query head (grid.z splits the tile's key range for the
+// exact tail). 192 threads:
+//   warp 0      producer: Q, and every contiguous (sink/window) K/V tile by TMA (128B swizzle);
+//               routed K/V rows gathered with cp.async into the same swizzled layout.
+//   warp 1      allocates TMEM and issues the MMAs from one thread:
+//                 S_j = Q K_j^T   (SS: A = Q smem K-major, B = K smem K-major) into S[j % 2]
+//                 O  += P_j V_j   (TS: A = P in TMEM over S[j % 2], B = V smem MN-major) into O
+//               S_{j+1} is issued before O += P_j V_j so the tensor core overlaps the softmax.
+//   warps 2-5   softmax: thread i owns query row i = TMEM lane i. It reads S with tcgen05.ld,
+//               masks edge tiles, updates the running max lazily (O in TMEM is rescaled only
+//               when the max grows by more than 2^8, so P <= 256), writes P as packed 16-bit
+//               pairs over S with tcgen05.st, and finally normalises O into the output.
+// TMEM: S[0] = columns 0-127, S[1] = 128-255, O = 256-383 (512 allocated; one CTA per SM).
+// Shared memory: Q 32 KB + a ring of NB = 4 tiles of 32 KB that alternately hold K_j and V_j.
+//
+// Every mbarrier wait is bounded (~2 s): on expiry the CTA raises an abort flag and the device
+// fault word, every role leaves its loop, in-flight copies and MMAs are drained (bounded), TMEM is
+// freed and the kernel returns.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "flash.cuh"
+
+namespace bb {
+
+__device__ int g_bb_fault = 0;
+
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int THREADS = 192;
+constexpr int NB = 4;
+constexpr uint32_t TILE = 32768u;   // 128 rows x 128 columns x 2 bytes
+constexpr uint32_t HALF = 16384u;   // 128 rows x 64 columns (one 128-byte swizzle span per row)
+constexpr float RESCALE_LOG2 = 8.0f;
+
+constexpr uint32_t SM_Q = 0;
+constexpr uint32_t SM_KV = TILE;
+constexpr uint32_t SM_POS = SM_KV + NB * TILE;  // [2][128] int32 routed-tile positions
+enum { B_Q = 0, B_FULL = 1, B_EMPTY = B_FULL + NB, B_S = B_EMPTY + NB, B_P = B_S + 2, B_O = B_P + 2,
+       B_DONE = B_O + 1, N_BARS = B_DONE + 1 };
+constexpr uint32_t SM_BAR = SM_POS + 2 * 128 * 4;
+constexpr uint32_t SM_MISC = SM_BAR + N_BARS * 8;  // [0] TMEM base, [1] abort flag
+constexpr uint32_t SM_BYTES = SM_MISC + 16;
+constexpr uint32_t SM_ALLOC = SM_BYTES + 1024;     // slack to align the base to 1024 bytes
+
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t COL_O = 256;
+
+// Fault codes written to g_bb_fault (which wait gave up).
+enum { F_SOFTMAX_S = 1, F_SOFTMAX_O = 2, F_MMA_Q = 3, F_MMA_K = 4, F_MMA_P = 5, F_MMA_V = 6,
+       F_PROD_EMPTY = 7, F_EPI_O = 8 };
+
+// ----------------------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
+
+// Waits for the phase of `parity`; false if another role aborted or ~2 s passed (then aborts).
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag, int code) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = gtimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 63) == 0) {
+      if (*abort_flag) return false;
+      if (gtimer() - t0 > WAIT_LIMIT_NS) {
+        *abort_flag = 1;
+        atomicExch(&g_bb_fault, code);
+        return false;
+      }
+    }
+  }
+}
+// Bounded wait used while draining on the way out (ignores the abort flag).
+__device__ __noinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = gtimer();
+  while (!mbar_try(bar, parity))
+    if (gtimer() - t0 > WAIT_LIMIT_NS) return;
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (tcgen05): start >> 4 at [0,14), LBO >> 4 at [16,30), SBO >> 4
+// at [32,46), fixed 0b01 at [46,48), swizzle mode at [61,64) (2 = 128-byte swizzle).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+// K-major, 128B-swizzled: 8-row core groups 1024 bytes apart; LBO unused.
+__device__ __forceinline__ uint64_t desc_k(uint32_t saddr) { return sdesc(saddr, 16, 1024); }
+// MN-major, 128B-swizzled: 64-element column blocks 16 KB apart (LBO), 8-row groups 1024 bytes (SBO).
+__device__ __forceinline__ uint64_t desc_mn(uint32_t saddr) { return sdesc(saddr, HALF, 1024); }
+
+// Instruction descriptor, kind::f16: D f32 (bit 4), A/B type at [7,10)/[10,13) (0 f16, 1 bf16),
+// B major at bit 16 (1 = MN), N >> 3 at [17,23), M >> 4 at [24,29).
+template <typename T> __host__ __device__ constexpr uint32_t ab_fmt();
+template <> __host__ __device__ constexpr uint32_t ab_fmt<__nv_bfloat16>() { return 1u; }
+template <> __host__ __device__ constexpr uint32_t ab_fmt<__half>() { return 0u; }
+template <typename T> __host__ __device__ constexpr uint32_t idesc(bool b_mn) {
+  return (1u << 4) | (ab_fmt<T>() << 7) | (ab_fmt<T>() << 10) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+      ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
+      ::"r"(d), "r"(a_tmem), "l"(b), "r"(id), "r"(acc));
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns -> 32 registers per thread (load and wait together,
+// so no use of the registers can be scheduled before the data has arrived).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n"
+      ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void named_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// ----------------------------------------------------------------------------- tile schedule
+// Tiles of one query tile, in order: contiguous key tiles (aligned to 128, covering the sink
+// [0, front) and the window [q_first - W + 1, q_last]; two ranges, merged when they touch), then
+// cdiv(route_k, 128) routed tiles for each route group touched by the query rows.
+struct Sched {
+  int64_t q_first, q_last;
+  int n_a, w_lo, n_w, n_contig;   // contiguous tile indices: [0, n_a) and [w_lo, w_lo + n_w)
+  int64_t g_lo;
+  int n_rpg, n_groups, total;
+};
+
+struct Tile {
+  int kind;        // 0 contiguous, 1 routed
+  int64_t k0;      // first key (contiguous)
+  int64_t group, slot0;
+  bool masked;
+};
+
+__device__ __forceinline__ Sched make_sched(const FlashParams& p, int64_t row0, int64_t row1) {
+  Sched s;
+  s.q_first = p.offset + row0;
+  s.q_last = p.offset + row1 - 1;
+  const int64_t sink_end = min(p.front, s.q_last + 1);
+  int n_a = sink_end > 0 ? (int)cdiv(sink_end, BN) : 0;
+  const int64_t wl = max(s.q_first - p.window + 1, (int64_t)0) / BN;
+  const int64_t wh = s.q_last / BN + 1;
+  int w_lo = (int)wl, n_w = (int)(wh - wl);
+  if (w_lo <= n_a) {  // ranges touch: one range [0, wh)
+    n_a = (int)max((int64_t)n_a, wh);
+    n_w = 0;
+    w_lo = n_a;
+  }
+  s.n_a = n_a;
+  s.w_lo = w_lo;
+  s.n_w = n_w;
+  s.n_contig = n_a + n_w;
+  s.n_rpg = (int)cdiv(p.route_k, BN);
+  s.g_lo = s.q_first / p.route_chunk;
+  const int64_t g_hi = min(s.q_last / p.route_chunk, p.route_groups - 1);
+  s.n_groups = (p.route_k > 0 && g_hi >= s.g_lo) ? (int)(g_hi - s.g_lo + 1) : 0;
+  s.total = s.n_contig + s.n_groups * s.n_rpg;
+  return s;
+}
+
+__device__ __forceinline__ Tile tile_at(const FlashParams& p, const Sched& s, int t) {
+  Tile tl;
+  tl.group = 0;
+  tl.slot0 = 0;
+  if (t < s.n_contig) {
+    tl.kind = 0;
+    tl.k0 = (int64_t)(t < s.n_a ? t : s.w_lo + (t - s.n_a)) * BN;
+    // Unmasked iff every key of the tile is valid for every row of the query tile.
+    const bool causal_ok = tl.k0 + BN - 1 <= s.q_first;
+    const bool sink_all = tl.k0 + BN <= p.front;
+    const bool window_all = tl.k0 >= s.q_last - p.window + 1;
+    tl.masked = !(causal_ok && (sink_all || window_all)) || p.mask != nullptr;
+  } else {
+    const int r = t - s.n_contig;
+    tl.kind = 1;
+    tl.k0 = 0;
+    tl.group = s.g_lo + r / s.n_rpg;
+    tl.slot0 = (int64_t)(r % s.n_rpg) * BN;
+    tl.masked = true;
+  }
+  return tl;
+}
+
+// Position of routed slot `slot` of `group` for head h, or -1 when empty / out of range.
+__device__ __forceinline__ int64_t routed_pos(const FlashParams& p, int64_t h, int64_t group, int64_t slot) {
+  if (slot >= p.route_k) return -1;
+  const int64_t ps = p.idx[h * p.si_h + group * p.si_g + slot * p.si_k];
+  return (ps < 0 || ps >= p.n) ? -1 : ps;
+}
+
+struct TcMaps {
+  CUtensorMap q, k, v;
+  int q_swap, kv_swap;  // 1: the map's dims are {d, heads, rows} (coordinates swapped)
+};
+
+template <typename T>
+__global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_constant__ TcMaps maps, FlashParams p) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sbase = (raw + 1023u) & ~1023u;
+  unsigned char* sptr = smem_raw + (sbase - raw);
+  volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(sptr + SM_MISC);
+  volatile uint32_t* abort_flag = misc + 1;
+  int32_t* pos_s = reinterpret_cast<int32_t*>(sptr + SM_POS);
+  auto bar = [&](int i) { return sbase + SM_BAR + 8u * (uint32_t)i; };
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t h = blockIdx.y;
+  const int split = blockIdx.z;
+  const int64_t row0 = p.row_begin + (int64_t)blockIdx.x * BM;
+  const int64_t row1 = min(row0 + BM, p.row_end);
+  const int64_t kvh = (h / p.num_heads) * (p.num_heads / p.kv_groups) + (h % p.num_heads) / p.kv_groups;
+  const int64_t batch = h / p.num_heads;
+  const Sched sc = make_sched(p, row0, row1);
+  const int t_begin = (int)((int64_t)sc.total * split / p.splits);
+  const int nt = (int)((int64_t)sc.total * (split + 1) / p.splits) - t_begin;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(B_Q), 1);
+    for (int i = 0; i < NB; ++i) {
+      mbar_init(bar(B_FULL + i), 1);
+      mbar_init(bar(B_EMPTY + i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(B_S + i), 1);
+      mbar_init(bar(B_P + i), 128);
+    }
+    mbar_init(bar(B_O), 1);
+    mbar_init(bar(B_DONE), 1);
+    misc[1] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sbase + SM_MISC),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = misc[0];
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    int fills[NB];
+#pragma unroll
+    for (int i = 0; i < NB; ++i) fills[i] = 0;
+    bool q_issued = false;
+    if (nt > 0) {
+      if (lane == 0) {
+        const int qc1 = (int)row0, qc2 = (int)h;
+        mbar_expect_tx(bar(B_Q), TILE);
+        if (maps.q_swap) {
+          tma_load_3d(sbase + SM_Q, &maps.q, 0, qc2, qc1, bar(B_Q));
+          tma_load_3d(sbase + SM_Q + HALF, &maps.q, 64, qc2, qc1, bar(B_Q));
+        } else {
+          tma_load_3d(sbase + SM_Q, &maps.q, 0, qc1, qc2, bar(B_Q));
+          tma_load_3d(sbase + SM_Q + HALF, &maps.q, 64, qc1, qc2, bar(B_Q));
+        }
+      }
+      q_issued = true;
+      const T* kbase = static_cast<const T*>(p.k) + kvh * p.sk_h;
+      const T* vbase = static_cast<const T*>(p.v) + kvh * p.sv_h;
+      for (int it = 0; it < 2 * nt; ++it) {
+        const int j = it >> 1;
+        const bool is_v = it & 1;
+        const int b = it % NB;
+        const int round = it / NB;
+        if (round > 0 && !mbar_wait(bar(B_EMPTY + b), (round - 1) & 1, abort_flag, F_PROD_EMPTY)) break;
+        const Tile tl = tile_at(p, sc, t_begin + j);
+        const uint32_t dst = sbase + SM_KV + (uint32_t)b * TILE;
+        if (tl.kind == 0) {
+          if (lane == 0) {
+            const CUtensorMap* m = is_v ? &maps.v : &maps.k;
+            const int c1 = (int)tl.k0, c2 = (int)kvh;
+            mbar_expect_tx(bar(B_FULL + b), TILE);
+            if (maps.kv_swap) {
+              tma_load_3d(dst, m, 0, c2, c1, bar(B_FULL + b));
+              tma_load_3d(dst + HALF, m, 64, c2, c1, bar(B_FULL + b));
+            } else {
+              tma_load_3d(dst, m, 0, c1, c2, bar(B_FULL + b));
+              tma_load_3d(dst + HALF, m, 64, c1, c2, bar(B_FULL + b));
+            }
+          }
+        } else {
+          // Gather 128 routed rows (16 chunks of 16 bytes each) into the 128B-swizzled layout.
+          const T* src_base = is_v ? vbase : kbase;
+          const int64_t sstride = is_v ? p.sv_t : p.sk_t;
+          for (int r = lane; r < BN; r += 32) {
+            const int64_t ps = routed_pos(p, h, tl.group, tl.slot0 + r);
+            const T* row = src_base + (ps < 0 ? 0 : ps) * sstride;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              const uint32_t d = dst + (uint32_t)(c >> 3) * HALF + (uint32_t)r * 128u +
+                                 (uint32_t)(((c & 7) ^ (r & 7)) << 4);
+              cp_async_16(d, row + c * 8, ps >= 0);
+            }
+          }
+          asm volatile("cp.async.wait_all;" ::: "memory");
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B_FULL + b));
+        }
+        ++fills[b];
+      }
+    }
+    // Drain: no copy may still be writing this CTA's shared memory when it exits.
+    if (lane == 0) {
+      if (q_issued) mbar_drain(bar(B_Q), 0);
+      for (int b = 0; b < NB; ++b)
+        if (fills[b] > 0) mbar_drain(bar(B_FULL + b), (fills[b] - 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0 && nt > 0) {
+      constexpr uint32_t ID_QK = idesc<T>(false), ID_PV = idesc<T>(true);
+      bool ok = mbar_wait(bar(B_Q), 0, abort_flag, F_MMA_Q);
+      auto issue_pv = [&](int i) -> bool {
+        if (!mbar_wait(bar(B_P + (i & 1)), (i >> 1) & 1, abort_flag, F_MMA_P)) return false;
+        const int itv = 2 * i + 1, bv = itv % NB;
+        if (!mbar_wait(bar(B_FULL + bv), (itv / NB) & 1, abort_flag, F_MMA_V)) return false;
+        tc_fence_after();
+        const uint32_t vb = sbase + SM_KV + (uint32_t)bv * TILE;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          mma_ts(tmem + COL_O, tmem + (uint32_t)(i & 1) * 128u + (uint32_t)k * 8u, desc_mn(vb + (uint32_t)k * 2048u),
+                 ID_PV, (i > 0 || k > 0) ? 1u : 0u);
+        mma_commit(bar(B_O));
+        mma_commit(bar(B_EMPTY + bv));
+        return true;
+      };
+      for (int j = 0; ok && j < nt; ++j) {
+        const int itk = 2 * j, bk = itk % NB;
+        if (!mbar_wait(bar(B_FULL + bk), (itk / NB) & 1, abort_flag, F_MMA_K)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t kb = sbase + SM_KV + (uint32_t)bk * TILE;
+        const uint32_t ds = tmem + (uint32_t)(j & 1) * 128u;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (uint32_t)(k >> 2) * HALF + (uint32_t)(k & 3) * 32u;
+          mma_ss(ds, desc_k(sbase + SM_Q + off), desc_k(kb + off), ID_QK, k > 0 ? 1u : 0u);
+        }
+        mma_commit(bar(B_S + (j & 1)));
+        mma_commit(bar(B_EMPTY + bk));
+        if (j > 0) ok = issue_pv(j - 1);
+      }
+      if (ok) issue_pv(nt - 1);
+      mma_commit(bar(B_DONE));
+      mbar_drain(bar(B_DONE), 0);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const uint32_t tl_lane = tmem + ((uint32_t)(wq * 32) << 16);
+    const int64_t qpos = p.offset + row0 + row;
+    const int64_t qgroup = qpos / p.route_chunk;
+    const float c = p.scale_log2;
+    float m_ref = -1.0e20f, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      const Tile tl = tile_at(p, sc, t_begin + j);
+      int32_t* ps_s = pos_s + (j & 1) * 128;
+      if (tl.kind == 1) {
+        ps_s[row] = (int32_t)routed_pos(p, h, tl.group, tl.slot0 + row);
+        named_sync(1, 128);
+      }
+      if (!mbar_wait(bar(B_S + (j & 1)), (j >> 1) & 1, abort_flag, F_SOFTMAX_S)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[128];
+      const uint32_t scol = tl_lane + (uint32_t)(j & 1) * 128u;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(scol + q4 * 32, s + q4 * 32);
+      if (tl.masked) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          bool valid;
+          int64_t ps;
+          if (tl.kind == 0) {
+            ps = tl.k0 + i;
+            valid = ps <= qpos && (ps < p.front || ps >= qpos - p.window + 1);
+          } else {
+            ps = ps_s[i];
+            valid = ps >= p.front && ps <= qpos && ps < qpos - p.window + 1 && qgroup == tl.group;
+          }
+          if (valid && p.mask) valid = p.mask[batch * p.sm_b + ps * p.sm_t] != 0;
+          if (!valid) s[i] = -INFINITY;
+        }
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, s[i]);
+      const float mt = mx * c;
+      if (j > 0 && !mbar_wait(bar(B_O), (j - 1) & 1, abort_flag, F_SOFTMAX_O)) {
+        ok = false;
+        break;
+      }
+      if (mt > m_ref + RESCALE_LOG2) {
+        const float alpha = fast_exp2(m_ref - mt);
+        if (j > 0 && m_ref > -1.0e20f) {
+          tc_fence_after();
+#pragma unroll 1
+          for (int q4 = 0; q4 < 4; ++q4) {
+            float o[32];
+            tmem_ld32(tl_lane + COL_O + q4 * 32, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(tl_lane + COL_O + q4 * 32, o);
+          }
+          tmem_wait_st();
+        }
+        l *= alpha;
+        m_ref = mt;
+      }
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float a = fast_exp2(fmaf(s[q4 * 32 + 2 * i], c, -m_ref));
+          const float b = fast_exp2(fmaf(s[q4 * 32 + 2 * i + 1], c, -m_ref));
+          l += a + b;
+          pk[i] = pack2<T>(a, b);
+        }
+        tmem_st16(scol + q4 * 16, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(B_P + (j & 1)));
+      if (tl.kind == 1) named_sync(1, 128);  // ps_s[(j & 1)] is rewritten two tiles later
+    }
+    // Epilogue: wait for the last P.V, normalise, store.
+    bool have_o = false;
+    if (ok && nt > 0) have_o = mbar_wait(bar(B_O), (nt - 1) & 1, abort_flag, F_EPI_O);
+    tc_fence_after();
+    const int64_t lrow = row0 + row;
+    const bool store = lrow < row1;
+    if (p.splits > 1) {
+      float* acc = p.part_acc + (((int64_t)split * p.bh + h) * p.t + lrow) * 128;
+      if (store) p.part_ml[((int64_t)split * p.bh + h) * p.t + lrow] = make_float2(have_o ? m_ref : -1.0e20f, have_o ? l : 0.f);
+#pragma unroll 1
+      for (int q4 = 0; q4 < 4; ++q4) {
+        float o[32];
+        if (have_o) {
+          tmem_ld32(tl_lane + COL_O + q4 * 32, o);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (store) {
+          float4* dst = reinterpret_cast<float4*>(acc + q4 * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        }
+      }
+    } else {
+      float inv = (have_o && l > 0.f) ? 1.f / fmaxf(l, 1.0e-20f) : 0.f;
+      if (p.mask && store && qpos < p.n && !p.mask[batch * p.sm_b + qpos * p.sm_t]) inv = 0.f;
+      T* out = static_cast<T*>(p.out) + h * p.so_h + lrow * p.so_t;
+#pragma unroll 1
+      for (int q4 = 0; q4 < 4; ++q4) {
+        float o[32];
+        if (have_o) {
+          tmem_ld32(tl_lane + COL_O + q4 * 32, o);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (store) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk[i] = pack2<T>(o[2 * i] * inv, o[2 * i + 1] * inv);
+          uint4* dst = reinterpret_cast<uint4*>(out + q4 * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// Merges the split partials of a 128-wide head: one warp per row, 4 columns per lane.
+template <typename T>
+__global__ void __launch_bounds__(128) tc_combine_kernel(FlashParams p) {
+  using E = Elem<T>;
+  const int64_t h = blockIdx.y;
+  const int64_t row = p.row_begin + (int64_t)blockIdx.x * 4 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= p.row_end) return;
+  float M = -INFINITY;
+  for (int s = 0; s < p.splits; ++s) M = fmaxf(M, p.part_ml[((int64_t)s * p.bh + h) * p.t + row].x);
+  float L = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < p.splits; ++s) {
+    const int64_t base = ((int64_t)s * p.bh + h) * p.t + row;
+    const float2 ml = p.part_ml[base];
+    const float w = fast_exp2(ml.x - M);
+    L += ml.y * w;
+    const float4 a = reinterpret_cast<const float4*>(p.part_acc + base * 128)[lane];
+    acc.x += a.x * w;
+    acc.y += a.y * w;
+    acc.z += a.z * w;
+    acc.w += a.w * w;
+  }
+  float inv = 1.f / fmaxf(L, 1.0e-20f);
+  const int64_t qpos = p.offset + row;
+  const int64_t batch = h / p.num_heads;
+  if (p.mask && !p.mask[batch * p.sm_b + qpos * p.sm_t]) inv = 0.f;
+  T* ob = static_cast<T*>(p.out) + h * p.so_h + row * p.so_t + lane * 4;
+  uint2 v;
+  v.x = pack2<T>(acc.x * inv, acc.y * inv);
+  v.y = pack2<T>(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2*>(ob) = v;
+}
+
+// ----------------------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// 3-D map over a [heads][rows][128] view with element strides (s_head, s_row); the two outer
+// dimensions are ordered by stride (swap = 1 when the head stride is the smaller one).
+int make_map(CUtensorMap* m, int* swap, const void* base, int dtype, int64_t heads, int64_t rows,
+             int64_t s_head, int64_t s_row) {
+  auto fn = encode_fn();
+  if (!fn) return fail(BB_ERR_DEVICE, "flash: cuTensorMapEncodeTiled is unavailable");
+  if (heads == 1) s_head = s_row * rows;
+  const bool sw = s_head < s_row;
+  *swap = sw ? 1 : 0;
+  cuuint64_t dims[3] = {128, (cuuint64_t)(sw ? heads : rows), (cuuint64_t)(sw ? rows : heads)};
+  cuuint64_t strides[2] = {(cuuint64_t)((sw ? s_head : s_row) * 2), (cuuint64_t)((sw ? s_row : s_head) * 2)};
+  cuuint32_t box[3] = {64, sw ? 1u : 128u, sw ? 128u : 1u};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, dtype == BB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(BB_ERR_LAUNCH, "flash: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return BB_OK;
+}
+
+template <typename T>
+int launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream) {
+  TcMaps maps;
+  const int64_t hk = a->bh / a->kv_groups;
+  int st = make_map(&maps.q, &maps.q_swap, a->q, a->dtype, a->bh, a->t, a->sq_h, a->sq_t);
+  if (st) return st;
+  int sk = 0, sv = 0;
+  st = make_map(&maps.k, &sk, a->k, a->dtype, hk, a->n, a->sk_h, a->sk_t);
+  if (st) return st;
+  st = make_map(&maps.v, &sv, a->v, a->dtype, hk, a->n, a->sv_h, a->sv_t);
+  if (st) return st;
+  if (sk != sv) return fail(BB_ERR_STRIDE, "flash: K and V views must have the same dimension order");
+  maps.kv_swap = sk;
+  cudaFuncSetAttribute(flash_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SM_ALLOC);
+  dim3 grid((unsigned)cdiv(a->row_end - a->row_begin, BM), (unsigned)a->bh, (unsigned)p.splits);
+  flash_tc_kernel<T><<<grid, THREADS, SM_ALLOC, stream>>>(maps, p);
+  BB_CHECK_LAUNCH("flash_tc_kernel");
+  if (p.splits > 1) {
+    dim3 g2((unsigned)cdiv(a->row_end - a->row_begin, 4), (unsigned)a->bh);
+    tc_combine_kernel<T><<<g2, 128, 0, stream>>>(p);
+    BB_CHECK_LAUNCH("tc_combine_kernel");
+  }
+  return BB_OK;
+}
+
+}  // namespace tc
+
+int flash_tc_splits(const bb_flash_args* a, int sms) {
+  const int64_t rows = a->row_end - a->row_begin;
+  const int64_t ctas = cdiv(rows, tc::BM) * a->bh;
+  const int64_t tiles = cdiv(std::min(a->n, a->window + tc::BM), tc::BN) + cdiv(a->front, tc::BN) +
+                        cdiv(a->route_k, tc::BN);
+  if (ctas <= 0 || ctas >= 2LL * sms || tiles < 16) return 1;
+  int best = 1;
+  int64_t best_cost = cdiv(ctas, sms) * tiles;
+  for (int s = 2; s <= 32 && s * 4 <= tiles; ++s) {
+    const int64_t cost = cdiv(ctas * s, sms) * cdiv(tiles, s) + 2;  // +2: split overhead
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
+}
+
+int flash_tc_launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream) {
+  if (a->dtype == BB_BF16) return tc::launch<__nv_bfloat16>(a, p, stream);
+  return tc::launch<__half>(a, p, stream);
+}
+
+int device_fault_take(int* code) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_bb_fault, sizeof(int));
+  if (e != cudaSuccess) return fail(BB_ERR_LAUNCH, "device_fault: %s", cudaGetErrorString(e));
+  if (v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_bb_fault, &zero, sizeof(int));
+  }
+  *code = v;
+  return BB_OK;
+}
+
+}  // namespace bb
