@@ -368,6 +368,10 @@ int launch_flash_t(const bb_flash_args* a, FlashParams& p, cudaStream_t stream) 
 
 }  // namespace
 
+// head_dim 128 without a token mask (every Llama-shaped layer) runs on the tcgen05/TMEM kernels;
+// smaller head dims and token-masked calls (the reference's exp 19 caller) run on the mma.sync kernel.
+bool use_tc(const bb_flash_args* a) { return a->d == 128 && a->token_mask == nullptr; }
+
 int flash_check(const bb_flash_args* a) {
   if (!a) return fail(BB_ERR_ARG, "flash: null args");
   if (a->dtype != BB_BF16 && a->dtype != BB_F16) return fail(BB_ERR_DTYPE, "flash: dtype must be f16 or bf16");
@@ -387,14 +391,12 @@ int flash_check_pointers(const bb_flash_args* a) {
   if (!al(a->q) || !al(a->k) || !al(a->v) || (a->sq_h * 2) % 16 || (a->sq_t * 2) % 16 ||
       (a->sk_h * 2) % 16 || (a->sk_t * 2) % 16 || (a->sv_h * 2) % 16 || (a->sv_t * 2) % 16)
     return fail(BB_ERR_STRIDE, "flash: q/k/v rows must start on 16-byte boundaries");
-  if (a->d == 128 && (!al(a->out) || (a->so_h * 2) % 16 || (a->so_t * 2) % 16))
+  if (use_tc(a) && (!al(a->out) || (a->so_h * 2) % 16 || (a->so_t * 2) % 16))
     return fail(BB_ERR_STRIDE, "flash: output rows must start on 16-byte boundaries");
   return BB_OK;
 }
 
-// head_dim 128 (every Llama-shaped layer) runs on the tcgen05/TMEM kernel; smaller head dims
-// (the reference's unit-test shapes) run on the mma.sync kernel.
-bool use_tc(const bb_flash_args* a) { return a->d == 128; }
+
 
 int splits_of(const bb_flash_args* a) { return use_tc(a) ? flash_tc_splits(a, num_sms()) : choose_splits(a); }
 

@@ -202,6 +202,58 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+#define BB_R8(b) "=r"(r[b]), "=r"(r[b + 1]), "=r"(r[b + 2]), "=r"(r[b + 3]), "=r"(r[b + 4]), "=r"(r[b + 5]), \
+                 "=r"(r[b + 6]), "=r"(r[b + 7])
+#define BB_W8(b) "r"(r[b]), "r"(r[b + 1]), "r"(r[b + 2]), "r"(r[b + 3]), "r"(r[b + 4]), "r"(r[b + 5]), \
+                 "r"(r[b + 6]), "r"(r[b + 7])
+
+// One row of a 128-column S tile: a single x128 load and its wait in one asm statement.
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, float* v) {
+  uint32_t r[128];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {"
+      "%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,"
+      "%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,"
+      "%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,"
+      "%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,"
+      "%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,"
+      "%121,%122,%123,%124,%125,%126,%127}, [%128];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : BB_R8(0), BB_R8(8), BB_R8(16), BB_R8(24), BB_R8(32), BB_R8(40), BB_R8(48), BB_R8(56), BB_R8(64),
+        BB_R8(72), BB_R8(80), BB_R8(88), BB_R8(96), BB_R8(104), BB_R8(112), BB_R8(120)
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 128; ++i) v[i] = __uint_as_float(r[i]);
+}
+// Half a row of S (64 columns): one x64 load and its wait.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
+      "%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,"
+      "%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,"
+      "%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : BB_R8(0), BB_R8(8), BB_R8(16), BB_R8(24), BB_R8(32), BB_R8(40), BB_R8(48), BB_R8(56)
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+// 64 packed columns (P of one row) in one store.
+__device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {"
+      "%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,"
+      "%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,"
+      "%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64};\n"
+      ::"r"(taddr), BB_W8(0), BB_W8(8), BB_W8(16), BB_W8(24), BB_W8(32), BB_W8(40), BB_W8(48), BB_W8(56)
+      : "memory");
+}
+#undef BB_R8
+#undef BB_W8
+
 __device__ __forceinline__ void named_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
@@ -278,6 +330,66 @@ __device__ __forceinline__ int64_t routed_pos(const FlashParams& p, int64_t h, i
   if (slot >= p.route_k) return -1;
   const int64_t ps = p.idx[h * p.si_h + group * p.si_g + slot * p.si_k];
   return (ps < 0 || ps >= p.n) ? -1 : ps;
+}
+
+// Masks one row of a 128-key tile. Contiguous tiles (kind 0, first key k0): key k0 + i is valid
+// iff k0 + i <= q and (k0 + i < front or k0 + i >= q - W + 1). Routed tiles (kind 1): slot i's
+// key ps (-1 = empty) is valid iff front <= ps <= q - W and the row's route group is the tile's.
+// Bounds are folded into per-row int32 limits first (positions are < 2^31), so the per-element
+// work is two compares and a select. (Calls with a token mask run on the mma.sync kernel.)
+__device__ __forceinline__ void mask_row(float* s, int kind, int64_t k0, int64_t group, const FlashParams& p,
+                                         int64_t qpos, int64_t qgroup, const int32_t* ps_s, int64_t batch) {
+  if (kind == 0) {
+    const int hi = (int)max(min(qpos - k0, (int64_t)128), (int64_t)-1);
+    const int f = (int)max(min(p.front - k0, (int64_t)128), (int64_t)0);
+    const int lo = (int)max(min(qpos - p.window + 1 - k0, (int64_t)129), (int64_t)0);
+#pragma unroll
+    for (int i = 0; i < 128; ++i)
+      if (!(i <= hi && (i < f || i >= lo))) s[i] = -INFINITY;
+  } else {
+    const int hr = qgroup == group ? (int)max(min(qpos - p.window, (int64_t)0x7fffffff), (int64_t)-1) : -1;
+    const int fr = (int)min(p.front, (int64_t)0x7fffffff);
+#pragma unroll
+    for (int i = 0; i < 128; ++i) {
+      const int ps = ps_s[i];
+      if (!(ps >= fr && ps <= hr)) s[i] = -INFINITY;
+    }
+  }
+}
+
+// Per-row mask limits of a tile (see mask_row): contiguous tiles keep column i iff
+// i <= hi && (i < f || i >= lo); routed tiles keep slot i iff f <= ps_s[i] <= hi.
+struct MaskLimits {
+  int hi, f, lo;
+};
+__device__ __forceinline__ MaskLimits mask_limits(int kind, int64_t k0, int64_t group, const FlashParams& p,
+                                                  int64_t qpos, int64_t qgroup) {
+  MaskLimits m;
+  if (kind == 0) {
+    m.hi = (int)max(min(qpos - k0, (int64_t)128), (int64_t)-1);
+    m.f = (int)max(min(p.front - k0, (int64_t)128), (int64_t)0);
+    m.lo = (int)max(min(qpos - p.window + 1 - k0, (int64_t)129), (int64_t)0);
+  } else {
+    m.hi = qgroup == group ? (int)max(min(qpos - p.window, (int64_t)0x7fffffff), (int64_t)-1) : -1;
+    m.f = (int)min(p.front, (int64_t)0x7fffffff);
+    m.lo = 0;
+  }
+  return m;
+}
+// Masks columns 64*half .. 64*half+63 of a row held in s[0..63].
+__device__ __forceinline__ void mask_half(float* s, int half, int kind, const MaskLimits& m, const int32_t* ps_s) {
+  const int base = 64 * half;
+  if (kind == 0) {
+#pragma unroll
+    for (int i = 0; i < 64; ++i)
+      if (!(base + i <= m.hi && (base + i < m.f || base + i >= m.lo))) s[i] = -INFINITY;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const int ps = ps_s[base + i];
+      if (!(ps >= m.f && ps <= m.hi)) s[i] = -INFINITY;
+    }
+  }
 }
 
 struct TcMaps {
@@ -468,34 +580,31 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
       tc_fence_after();
       float s[128];
       const uint32_t scol = tl_lane + (uint32_t)(j & 1) * 128u;
+      tmem_ld128(scol, s);
+      if (tl.masked) mask_row(s, tl.kind, tl.k0, tl.group, p, qpos, qgroup, ps_s, batch);
+      // Row max as a tree (short dependency chains).
+      float mx8[8];
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(scol + q4 * 32, s + q4 * 32);
-      if (tl.masked) {
+      for (int k = 0; k < 8; ++k) mx8[k] = s[k];
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          bool valid;
-          int64_t ps;
-          if (tl.kind == 0) {
-            ps = tl.k0 + i;
-            valid = ps <= qpos && (ps < p.front || ps >= qpos - p.window + 1);
-          } else {
-            ps = ps_s[i];
-            valid = ps >= p.front && ps <= qpos && ps < qpos - p.window + 1 && qgroup == tl.group;
-          }
-          if (valid && p.mask) valid = p.mask[batch * p.sm_b + ps * p.sm_t] != 0;
-          if (!valid) s[i] = -INFINITY;
-        }
-      }
-      float mx = s[0];
+      for (int i = 8; i < 128; i += 8)
 #pragma unroll
-      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, s[i]);
+        for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], s[i + k]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float mt = mx * c;
-      if (j > 0 && !mbar_wait(bar(B_O), (j - 1) & 1, abort_flag, F_SOFTMAX_O)) {
-        ok = false;
-        break;
-      }
+      // The wait for P_{j-1} V_{j-1} (completion j of B_O) is taken in order every tile: here when
+      // O must be rescaled, otherwise after the exponentials, by when it has normally completed.
+      bool o_waited = j == 0;
       if (mt > m_ref + RESCALE_LOG2) {
         const float alpha = fast_exp2(m_ref - mt);
+        if (!o_waited) {
+          if (!mbar_wait(bar(B_O), (j - 1) & 1, abort_flag, F_SOFTMAX_O)) {
+            ok = false;
+            break;
+          }
+          o_waited = true;
+        }
         if (j > 0 && m_ref > -1.0e20f) {
           tc_fence_after();
 #pragma unroll 1
@@ -511,18 +620,22 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         l *= alpha;
         m_ref = mt;
       }
+      uint32_t pk[64];
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      const float neg = -m_ref;
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float a = fast_exp2(fmaf(s[q4 * 32 + 2 * i], c, -m_ref));
-          const float b = fast_exp2(fmaf(s[q4 * 32 + 2 * i + 1], c, -m_ref));
-          l += a + b;
-          pk[i] = pack2<T>(a, b);
-        }
-        tmem_st16(scol + q4 * 16, pk);
+      for (int i = 0; i < 64; ++i) {
+        const float a = fast_exp2(fmaf(s[2 * i], c, neg));
+        const float b = fast_exp2(fmaf(s[2 * i + 1], c, neg));
+        ls[i & 3] += a + b;
+        pk[i] = pack2<T>(a, b);
       }
+      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      if (!o_waited && !mbar_wait(bar(B_O), (j - 1) & 1, abort_flag, F_SOFTMAX_O)) {
+        ok = false;
+        break;
+      }
+      tmem_st64(scol, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(B_P + (j & 1)));
@@ -584,6 +697,395 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
   }
 }
 
+// ============================================================================= paired kernel
+// Two query heads of one KV head (a GQA pair, heads 2m and 2m+1) x 128 query rows per CTA. The
+// K/V tiles of the sink and window are loaded once for both heads; the routed tiles of head A and
+// then of head B follow (each head masks the other head's routed tiles entirely and writes P = 0
+// for them). Each head has its own softmax warpgroup, S buffer and O accumulator in TMEM:
+//   S_A = columns 0-127, S_B = 128-255, O_A = 256-383, O_B = 384-511.
+// The single MMA thread alternates  P_A V -> S_A(next) -> P_B V -> S_B(next), so while one
+// warpgroup runs its softmax the tensor core works for the other (ping-pong).
+// 320 threads (10 warps; at most 3 warps share an SM sub-partition's 16K registers, so 168
+// registers per thread): producer (warp 0), MMA issuer (warp 1),
+// softmax of head A (warps 2-5) and of head B (warps 6-9); warp w reads TMEM lanes
+// 32 * (w % 4) .. 32 * (w % 4) + 31, so each softmax group covers all 128 rows.
+constexpr int P_THREADS = 320;
+constexpr int PNB = 4;
+constexpr uint32_t P_SM_QA = 0;
+constexpr uint32_t P_SM_QB = TILE;
+constexpr uint32_t P_SM_KV = 2 * TILE;
+constexpr uint32_t P_SM_POS = P_SM_KV + PNB * TILE;  // [2 heads][128] int32 routed positions
+enum { PB_Q = 0, PB_FULL = 1, PB_EMPTY = PB_FULL + PNB, PB_S = PB_EMPTY + PNB, PB_P = PB_S + 2, PB_O = PB_P + 2,
+       PB_DONE = PB_O + 2, PN_BARS = PB_DONE + 1 };
+constexpr uint32_t P_SM_BAR = P_SM_POS + 2 * 128 * 4;
+constexpr uint32_t P_SM_MISC = P_SM_BAR + PN_BARS * 8;
+constexpr uint32_t P_SM_ALLOC = P_SM_MISC + 16 + 1024;
+
+struct Tile2 {
+  int kind;   // 0 contiguous (both heads), 1 routed
+  int owner;  // routed tiles: 0 = head A, 1 = head B
+  int64_t k0, group, slot0;
+  bool masked;
+};
+
+__device__ __forceinline__ Tile2 tile2_at(const FlashParams& p, const Sched& s, int t) {
+  Tile2 r;
+  if (t < s.n_contig) {
+    const Tile a = tile_at(p, s, t);
+    r.kind = 0;
+    r.owner = 0;
+    r.k0 = a.k0;
+    r.group = 0;
+    r.slot0 = 0;
+    r.masked = a.masked;
+  } else {
+    const int per_head = s.n_groups * s.n_rpg;
+    const int q = t - s.n_contig;
+    r.kind = 1;
+    r.owner = q / per_head;
+    const int rr = q % per_head;
+    r.k0 = 0;
+    r.group = s.g_lo + rr / s.n_rpg;
+    r.slot0 = (int64_t)(rr % s.n_rpg) * BN;
+    r.masked = true;
+  }
+  return r;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __grid_constant__ TcMaps maps,
+                                                                      FlashParams p) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sbase = (raw + 1023u) & ~1023u;
+  unsigned char* sptr = smem_raw + (sbase - raw);
+  volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(sptr + P_SM_MISC);
+  volatile uint32_t* abort_flag = misc + 1;
+  int32_t* pos_s = reinterpret_cast<int32_t*>(sptr + P_SM_POS);
+  auto bar = [&](int i) { return sbase + P_SM_BAR + 8u * (uint32_t)i; };
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t hA = 2 * (int64_t)blockIdx.y;
+  const int split = blockIdx.z;
+  const int64_t row0 = p.row_begin + (int64_t)blockIdx.x * BM;
+  const int64_t row1 = min(row0 + BM, p.row_end);
+  const int64_t kvh = (hA / p.num_heads) * (p.num_heads / p.kv_groups) + (hA % p.num_heads) / p.kv_groups;
+  Sched sc = make_sched(p, row0, row1);
+  sc.total = sc.n_contig + 2 * sc.n_groups * sc.n_rpg;
+  const int t_begin = (int)((int64_t)sc.total * split / p.splits);
+  const int nt = (int)((int64_t)sc.total * (split + 1) / p.splits) - t_begin;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(PB_Q), 1);
+    for (int i = 0; i < PNB; ++i) {
+      mbar_init(bar(PB_FULL + i), 1);
+      mbar_init(bar(PB_EMPTY + i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(PB_S + i), 1);
+      mbar_init(bar(PB_P + i), 128);
+      mbar_init(bar(PB_O + i), 1);
+    }
+    mbar_init(bar(PB_DONE), 1);
+    misc[1] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sbase + P_SM_MISC),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = misc[0];
+
+  if (warp < 2) {
+    if (warp == 0) {
+      // ---------------------------------------------------------------- producer
+      int fills[PNB];
+#pragma unroll
+      for (int i = 0; i < PNB; ++i) fills[i] = 0;
+      if (nt > 0) {
+        if (lane == 0) {
+          mbar_expect_tx(bar(PB_Q), 2 * TILE);
+          for (int w = 0; w < 2; ++w) {
+            const uint32_t dq = sbase + (w ? P_SM_QB : P_SM_QA);
+            const int c1 = (int)row0, c2 = (int)(hA + w);
+            if (maps.q_swap) {
+              tma_load_3d(dq, &maps.q, 0, c2, c1, bar(PB_Q));
+              tma_load_3d(dq + HALF, &maps.q, 64, c2, c1, bar(PB_Q));
+            } else {
+              tma_load_3d(dq, &maps.q, 0, c1, c2, bar(PB_Q));
+              tma_load_3d(dq + HALF, &maps.q, 64, c1, c2, bar(PB_Q));
+            }
+          }
+        }
+        const T* kbase = static_cast<const T*>(p.k) + kvh * p.sk_h;
+        const T* vbase = static_cast<const T*>(p.v) + kvh * p.sv_h;
+        for (int it = 0; it < 2 * nt; ++it) {
+          const int j = it >> 1;
+          const bool is_v = it & 1;
+          const int b = it % PNB;
+          const int round = it / PNB;
+          if (round > 0 && !mbar_wait(bar(PB_EMPTY + b), (round - 1) & 1, abort_flag, F_PROD_EMPTY)) break;
+          const Tile2 tl = tile2_at(p, sc, t_begin + j);
+          const uint32_t dst = sbase + P_SM_KV + (uint32_t)b * TILE;
+          if (tl.kind == 0) {
+            if (lane == 0) {
+              const CUtensorMap* m = is_v ? &maps.v : &maps.k;
+              const int c1 = (int)tl.k0, c2 = (int)kvh;
+              mbar_expect_tx(bar(PB_FULL + b), TILE);
+              if (maps.kv_swap) {
+                tma_load_3d(dst, m, 0, c2, c1, bar(PB_FULL + b));
+                tma_load_3d(dst + HALF, m, 64, c2, c1, bar(PB_FULL + b));
+              } else {
+                tma_load_3d(dst, m, 0, c1, c2, bar(PB_FULL + b));
+                tma_load_3d(dst + HALF, m, 64, c1, c2, bar(PB_FULL + b));
+              }
+            }
+          } else {
+            const T* src_base = is_v ? vbase : kbase;
+            const int64_t sstride = is_v ? p.sv_t : p.sk_t;
+            for (int r = lane; r < BN; r += 32) {
+              const int64_t ps = routed_pos(p, hA + tl.owner, tl.group, tl.slot0 + r);
+              const T* row = src_base + (ps < 0 ? 0 : ps) * sstride;
+#pragma unroll
+              for (int c = 0; c < 16; ++c) {
+                const uint32_t d = dst + (uint32_t)(c >> 3) * HALF + (uint32_t)r * 128u +
+                                   (uint32_t)(((c & 7) ^ (r & 7)) << 4);
+                cp_async_16(d, row + c * 8, ps >= 0);
+              }
+            }
+            asm volatile("cp.async.wait_all;" ::: "memory");
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(PB_FULL + b));
+          }
+          ++fills[b];
+        }
+      }
+      if (lane == 0) {
+        if (nt > 0) mbar_drain(bar(PB_Q), 0);
+        for (int b = 0; b < PNB; ++b)
+          if (fills[b] > 0) mbar_drain(bar(PB_FULL + b), (fills[b] - 1) & 1);
+      }
+    } else if (warp == 1 && lane == 0 && nt > 0) {
+      // ---------------------------------------------------------------- MMA issuer
+      constexpr uint32_t ID_QK = idesc<T>(false), ID_PV = idesc<T>(true);
+      auto s_mma = [&](int w, uint32_t kb) {
+        const uint32_t qs = sbase + (w ? P_SM_QB : P_SM_QA);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (uint32_t)(k >> 2) * HALF + (uint32_t)(k & 3) * 32u;
+          mma_ss(tmem + (uint32_t)w * 128u, desc_k(qs + off), desc_k(kb + off), ID_QK, k > 0 ? 1u : 0u);
+        }
+        mma_commit(bar(PB_S + w));
+      };
+      // O_w += P_w(i) V_i; `wait_v`: the first of the two heads also waits for V_i to land.
+      auto pv = [&](int w, int i, bool wait_v) -> bool {
+        if (!mbar_wait(bar(PB_P + w), i & 1, abort_flag, F_MMA_P)) return false;
+        const int itv = 2 * i + 1, bv = itv % PNB;
+        if (wait_v && !mbar_wait(bar(PB_FULL + bv), (itv / PNB) & 1, abort_flag, F_MMA_V)) return false;
+        tc_fence_after();
+        const uint32_t vb = sbase + P_SM_KV + (uint32_t)bv * TILE;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          mma_ts(tmem + 256u + (uint32_t)w * 128u, tmem + (uint32_t)w * 128u + (uint32_t)k * 8u,
+                 desc_mn(vb + (uint32_t)k * 2048u), ID_PV, (i > 0 || k > 0) ? 1u : 0u);
+        mma_commit(bar(PB_O + w));
+        return true;
+      };
+      bool ok = mbar_wait(bar(PB_Q), 0, abort_flag, F_MMA_Q);
+      for (int j = 0; ok && j < nt; ++j) {
+        const int itk = 2 * j, bk = itk % PNB;
+        if (!mbar_wait(bar(PB_FULL + bk), (itk / PNB) & 1, abort_flag, F_MMA_K)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t kb = sbase + P_SM_KV + (uint32_t)bk * TILE;
+        if (j > 0) {
+          if (!(ok = pv(0, j - 1, true))) break;
+          s_mma(0, kb);
+          if (!(ok = pv(1, j - 1, false))) break;
+          mma_commit(bar(PB_EMPTY + (2 * (j - 1) + 1) % PNB));  // V_{j-1} consumed by both heads
+          s_mma(1, kb);
+        } else {
+          s_mma(0, kb);
+          s_mma(1, kb);
+        }
+        mma_commit(bar(PB_EMPTY + bk));  // K_j consumed by both heads
+      }
+      if (ok && pv(0, nt - 1, true) && pv(1, nt - 1, false))
+        mma_commit(bar(PB_EMPTY + (2 * (nt - 1) + 1) % PNB));
+      mma_commit(bar(PB_DONE));
+      mbar_drain(bar(PB_DONE), 0);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int w = (warp - 2) >> 2;  // 0: head A, 1: head B
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const int64_t h = hA + w;
+    const int64_t batch = h / p.num_heads;
+    const uint32_t tl_lane = tmem + ((uint32_t)(wq * 32) << 16);
+    const uint32_t scol = tl_lane + (uint32_t)w * 128u;
+    const uint32_t ocol = tl_lane + 256u + (uint32_t)w * 128u;
+    const int64_t qpos = p.offset + row0 + row;
+    const int64_t qgroup = qpos / p.route_chunk;
+    int32_t* ps_s = pos_s + w * 128;
+    const float c = p.scale_log2;
+    float m_ref = -1.0e20f, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      const Tile2 tl = tile2_at(p, sc, t_begin + j);
+      const bool own = tl.kind == 0 || tl.owner == w;
+      if (own && tl.kind == 1) {
+        ps_s[row] = (int32_t)routed_pos(p, h, tl.group, tl.slot0 + row);
+        named_sync(1 + w, 128);
+      }
+      if (!mbar_wait(bar(PB_S + w), j & 1, abort_flag, F_SOFTMAX_S)) {
+        ok = false;
+        break;
+      }
+      // P_w(j-1) V_{j-1} was issued before S_w(j), so it has completed by now (in-order tensor
+      // pipe): this wait returns at once and keeps the O barrier's phases in step.
+      if (j > 0 && !mbar_wait(bar(PB_O + w), (j - 1) & 1, abort_flag, F_SOFTMAX_O)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (own) {
+        // Pass 1: row max over the two 64-column halves of S (re-read in pass 2, so only 64
+        // scores are live at a time and the softmax fits the 168-register budget).
+        const MaskLimits ml = tl.masked ? mask_limits(tl.kind, tl.k0, tl.group, p, qpos, qgroup)
+                                        : MaskLimits{127, 128, 0};
+        float mx8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          float s[64];
+          tmem_ld64(scol + 64u * half, s);
+          if (tl.masked) mask_half(s, half, tl.kind, ml, ps_s);
+#pragma unroll
+          for (int i = 0; i < 64; i += 8)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], s[i + k]);
+        }
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        const float mt = mx * c;
+        if (mt > m_ref + RESCALE_LOG2) {
+          const float alpha = fast_exp2(m_ref - mt);
+          if (j > 0 && m_ref > -1.0e20f) {
+#pragma unroll 1
+            for (int q4 = 0; q4 < 4; ++q4) {
+              float o[32];
+              tmem_ld32(ocol + q4 * 32, o);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] *= alpha;
+              tmem_st32(ocol + q4 * 32, o);
+            }
+          }
+          l *= alpha;
+          m_ref = mt;
+        }
+        // Pass 2: P = exp2(s * c - m_ref), written as packed 16-bit pairs over S columns
+        // [0, 64); half h of S (columns 64h..64h+63) becomes P columns 32h..32h+31, so the
+        // second half is read before anything overwrites it.
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
+        const float neg = -m_ref;
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          float s[64];
+          tmem_ld64(scol + 64u * half, s);
+          if (tl.masked) mask_half(s, half, tl.kind, ml, ps_s);
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float a = fast_exp2(fmaf(s[32 * q + 2 * i], c, neg));
+              const float b = fast_exp2(fmaf(s[32 * q + 2 * i + 1], c, neg));
+              ls[i & 3] += a + b;
+              pk[i] = pack2<T>(a, b);
+            }
+            tmem_st16(scol + 32u * half + 16u * q, pk);
+          }
+        }
+        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      } else {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = 0u;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) tmem_st16(scol + 16u * q4, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(PB_P + w));
+      if (own && tl.kind == 1) named_sync(1 + w, 128);
+    }
+    bool have_o = false;
+    if (ok && nt > 0) have_o = mbar_wait(bar(PB_O + w), (nt - 1) & 1, abort_flag, F_EPI_O);
+    tc_fence_after();
+    const int64_t lrow = row0 + row;
+    const bool store = lrow < row1;
+    if (p.splits > 1) {
+      float* acc = p.part_acc + (((int64_t)split * p.bh + h) * p.t + lrow) * 128;
+      if (store)
+        p.part_ml[((int64_t)split * p.bh + h) * p.t + lrow] =
+            make_float2(have_o ? m_ref : -1.0e20f, have_o ? l : 0.f);
+#pragma unroll 1
+      for (int q4 = 0; q4 < 4; ++q4) {
+        float o[32];
+        if (have_o) {
+          tmem_ld32(ocol + q4 * 32, o);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (store) {
+          float4* dst = reinterpret_cast<float4*>(acc + q4 * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        }
+      }
+    } else {
+      float inv = (have_o && l > 0.f) ? 1.f / fmaxf(l, 1.0e-20f) : 0.f;
+      if (p.mask && store && qpos < p.n && !p.mask[batch * p.sm_b + qpos * p.sm_t]) inv = 0.f;
+      T* out = static_cast<T*>(p.out) + h * p.so_h + lrow * p.so_t;
+#pragma unroll 1
+      for (int q4 = 0; q4 < 4; ++q4) {
+        float o[32];
+        if (have_o) {
+          tmem_ld32(ocol + q4 * 32, o);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (store) {
+          uint32_t q16[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) q16[i] = pack2<T>(o[2 * i] * inv, o[2 * i + 1] * inv);
+          uint4* dst = reinterpret_cast<uint4*>(out + q4 * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(q16[4 * i], q16[4 * i + 1], q16[4 * i + 2], q16[4 * i + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
 // Merges the split partials of a 128-wide head: one warp per row, 4 columns per lane.
 template <typename T>
 __global__ void __launch_bounds__(128) tc_combine_kernel(FlashParams p) {
@@ -619,6 +1121,11 @@ __global__ void __launch_bounds__(128) tc_combine_kernel(FlashParams p) {
 }
 
 // ----------------------------------------------------------------------------- host side
+// Two query heads per CTA when consecutive heads share a KV head (even GQA group size).
+bool pair_mode(const bb_flash_args* a) {
+  return a->kv_groups % 2 == 0 && a->num_heads % 2 == 0 && a->bh % 2 == 0;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static std::once_flag once;
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -665,10 +1172,17 @@ int launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream) {
   if (st) return st;
   if (sk != sv) return fail(BB_ERR_STRIDE, "flash: K and V views must have the same dimension order");
   maps.kv_swap = sk;
-  cudaFuncSetAttribute(flash_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SM_ALLOC);
-  dim3 grid((unsigned)cdiv(a->row_end - a->row_begin, BM), (unsigned)a->bh, (unsigned)p.splits);
-  flash_tc_kernel<T><<<grid, THREADS, SM_ALLOC, stream>>>(maps, p);
-  BB_CHECK_LAUNCH("flash_tc_kernel");
+  if (pair_mode(a)) {
+    cudaFuncSetAttribute(flash_tc_pair_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SM_ALLOC);
+    dim3 grid((unsigned)cdiv(a->row_end - a->row_begin, BM), (unsigned)(a->bh / 2), (unsigned)p.splits);
+    flash_tc_pair_kernel<T><<<grid, P_THREADS, P_SM_ALLOC, stream>>>(maps, p);
+    BB_CHECK_LAUNCH("flash_tc_pair_kernel");
+  } else {
+    cudaFuncSetAttribute(flash_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SM_ALLOC);
+    dim3 grid((unsigned)cdiv(a->row_end - a->row_begin, BM), (unsigned)a->bh, (unsigned)p.splits);
+    flash_tc_kernel<T><<<grid, THREADS, SM_ALLOC, stream>>>(maps, p);
+    BB_CHECK_LAUNCH("flash_tc_kernel");
+  }
   if (p.splits > 1) {
     dim3 g2((unsigned)cdiv(a->row_end - a->row_begin, 4), (unsigned)a->bh);
     tc_combine_kernel<T><<<g2, 128, 0, stream>>>(p);
@@ -681,9 +1195,10 @@ int launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream) {
 
 int flash_tc_splits(const bb_flash_args* a, int sms) {
   const int64_t rows = a->row_end - a->row_begin;
-  const int64_t ctas = cdiv(rows, tc::BM) * a->bh;
+  const bool pair = tc::pair_mode(a);
+  const int64_t ctas = cdiv(rows, tc::BM) * (pair ? a->bh / 2 : a->bh);
   const int64_t tiles = cdiv(std::min(a->n, a->window + tc::BM), tc::BN) + cdiv(a->front, tc::BN) +
-                        cdiv(a->route_k, tc::BN);
+                        (pair ? 2 : 1) * cdiv(a->route_k, tc::BN);
   if (ctas <= 0 || ctas >= 2LL * sms || tiles < 16) return 1;
   int best = 1;
   int64_t best_cost = cdiv(ctas, sms) * tiles;
