@@ -119,6 +119,25 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Issue-side wrappers for a converged warp: every lane executes the instruction with operands the
+// compiler can keep in uniform registers, and only the lane with `lead` != 0 (predicate) issues.
+__device__ __forceinline__ void mbar_expect_tx_if(uint32_t lead, uint32_t bar, uint32_t bytes) {
+  asm volatile("{\n .reg .pred q;\n setp.ne.b32 q, %2, 0;\n @q mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n}\n"
+               ::"r"(bar), "r"(bytes), "r"(lead) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_if(uint32_t lead, uint32_t bar) {
+  asm volatile("{\n .reg .pred q;\n setp.ne.b32 q, %1, 0;\n @q mbarrier.arrive.shared::cta.b64 _, [%0];\n}\n"
+               ::"r"(bar), "r"(lead) : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_if(uint32_t lead, uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                               int c2, uint32_t bar) {
+  asm volatile(
+      "{\n .reg .pred q;\n setp.ne.b32 q, %6, 0;\n"
+      " @q cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n}\n"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar), "r"(lead)
+      : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -156,6 +175,24 @@ __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, 
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
+}
+
+__device__ __forceinline__ void mma_ss_if(uint32_t lead, uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.b32 p, %4, 0;\n setp.ne.b32 q, %5, 0;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+      ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc), "r"(lead));
+}
+__device__ __forceinline__ void mma_ts_if(uint32_t lead, uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.b32 p, %4, 0;\n setp.ne.b32 q, %5, 0;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
+      ::"r"(d), "r"(a_tmem), "l"(b), "r"(id), "r"(acc), "r"(lead));
+}
+__device__ __forceinline__ void mma_commit_if(uint32_t lead, uint32_t bar) {
+  asm volatile("{\n .reg .pred q;\n setp.ne.b32 q, %1, 0;\n"
+               " @q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n"
+               ::"r"(bar), "r"(lead) : "memory");
 }
 
 // 32 lanes x 32 consecutive 32-bit columns -> 32 registers per thread (load and wait together,
@@ -447,20 +484,21 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
+    const uint32_t lead = lane == 0;
     int fills[NB];
 #pragma unroll
     for (int i = 0; i < NB; ++i) fills[i] = 0;
     bool q_issued = false;
     if (nt > 0) {
-      if (lane == 0) {
+      {
         const int qc1 = (int)row0, qc2 = (int)h;
-        mbar_expect_tx(bar(B_Q), TILE);
+        mbar_expect_tx_if(lead, bar(B_Q), TILE);
         if (maps.q_swap) {
-          tma_load_3d(sbase + SM_Q, &maps.q, 0, qc2, qc1, bar(B_Q));
-          tma_load_3d(sbase + SM_Q + HALF, &maps.q, 64, qc2, qc1, bar(B_Q));
+          tma_load_3d_if(lead, sbase + SM_Q, &maps.q, 0, qc2, qc1, bar(B_Q));
+          tma_load_3d_if(lead, sbase + SM_Q + HALF, &maps.q, 64, qc2, qc1, bar(B_Q));
         } else {
-          tma_load_3d(sbase + SM_Q, &maps.q, 0, qc1, qc2, bar(B_Q));
-          tma_load_3d(sbase + SM_Q + HALF, &maps.q, 64, qc1, qc2, bar(B_Q));
+          tma_load_3d_if(lead, sbase + SM_Q, &maps.q, 0, qc1, qc2, bar(B_Q));
+          tma_load_3d_if(lead, sbase + SM_Q + HALF, &maps.q, 64, qc1, qc2, bar(B_Q));
         }
       }
       q_issued = true;
@@ -475,16 +513,16 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         const Tile tl = tile_at(p, sc, t_begin + j);
         const uint32_t dst = sbase + SM_KV + (uint32_t)b * TILE;
         if (tl.kind == 0) {
-          if (lane == 0) {
+          {
             const CUtensorMap* m = is_v ? &maps.v : &maps.k;
             const int c1 = (int)tl.k0, c2 = (int)kvh;
-            mbar_expect_tx(bar(B_FULL + b), TILE);
+            mbar_expect_tx_if(lead, bar(B_FULL + b), TILE);
             if (maps.kv_swap) {
-              tma_load_3d(dst, m, 0, c2, c1, bar(B_FULL + b));
-              tma_load_3d(dst + HALF, m, 64, c2, c1, bar(B_FULL + b));
+              tma_load_3d_if(lead, dst, m, 0, c2, c1, bar(B_FULL + b));
+              tma_load_3d_if(lead, dst + HALF, m, 64, c2, c1, bar(B_FULL + b));
             } else {
-              tma_load_3d(dst, m, 0, c1, c2, bar(B_FULL + b));
-              tma_load_3d(dst + HALF, m, 64, c1, c2, bar(B_FULL + b));
+              tma_load_3d_if(lead, dst, m, 0, c1, c2, bar(B_FULL + b));
+              tma_load_3d_if(lead, dst + HALF, m, 64, c1, c2, bar(B_FULL + b));
             }
           }
         } else {
@@ -504,20 +542,21 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
           asm volatile("cp.async.wait_all;" ::: "memory");
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar(B_FULL + b));
+          mbar_arrive_if(lead, bar(B_FULL + b));
         }
         ++fills[b];
       }
     }
     // Drain: no copy may still be writing this CTA's shared memory when it exits.
-    if (lane == 0) {
+    {
       if (q_issued) mbar_drain(bar(B_Q), 0);
       for (int b = 0; b < NB; ++b)
         if (fills[b] > 0) mbar_drain(bar(B_FULL + b), (fills[b] - 1) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0 && nt > 0) {
+    if (nt > 0) {
+      const uint32_t lead = lane == 0;
       constexpr uint32_t ID_QK = idesc<T>(false), ID_PV = idesc<T>(true);
       bool ok = mbar_wait(bar(B_Q), 0, abort_flag, F_MMA_Q);
       auto issue_pv = [&](int i) -> bool {
@@ -528,10 +567,10 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         const uint32_t vb = sbase + SM_KV + (uint32_t)bv * TILE;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          mma_ts(tmem + COL_O, tmem + (uint32_t)(i & 1) * 128u + (uint32_t)k * 8u, desc_mn(vb + (uint32_t)k * 2048u),
+          mma_ts_if(lead, tmem + COL_O, tmem + (uint32_t)(i & 1) * 128u + (uint32_t)k * 8u, desc_mn(vb + (uint32_t)k * 2048u),
                  ID_PV, (i > 0 || k > 0) ? 1u : 0u);
-        mma_commit(bar(B_O));
-        mma_commit(bar(B_EMPTY + bv));
+        mma_commit_if(lead, bar(B_O));
+        mma_commit_if(lead, bar(B_EMPTY + bv));
         return true;
       };
       for (int j = 0; ok && j < nt; ++j) {
@@ -546,14 +585,14 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t off = (uint32_t)(k >> 2) * HALF + (uint32_t)(k & 3) * 32u;
-          mma_ss(ds, desc_k(sbase + SM_Q + off), desc_k(kb + off), ID_QK, k > 0 ? 1u : 0u);
+          mma_ss_if(lead, ds, desc_k(sbase + SM_Q + off), desc_k(kb + off), ID_QK, k > 0 ? 1u : 0u);
         }
-        mma_commit(bar(B_S + (j & 1)));
-        mma_commit(bar(B_EMPTY + bk));
+        mma_commit_if(lead, bar(B_S + (j & 1)));
+        mma_commit_if(lead, bar(B_EMPTY + bk));
         if (j > 0) ok = issue_pv(j - 1);
       }
       if (ok) issue_pv(nt - 1);
-      mma_commit(bar(B_DONE));
+      mma_commit_if(lead, bar(B_DONE));
       mbar_drain(bar(B_DONE), 0);
     }
   } else {
@@ -804,21 +843,22 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
   if (warp < 2) {
     if (warp == 0) {
       // ---------------------------------------------------------------- producer
+      const uint32_t lead = lane == 0;
       int fills[PNB];
 #pragma unroll
       for (int i = 0; i < PNB; ++i) fills[i] = 0;
       if (nt > 0) {
-        if (lane == 0) {
-          mbar_expect_tx(bar(PB_Q), 2 * TILE);
+        {
+          mbar_expect_tx_if(lead, bar(PB_Q), 2 * TILE);
           for (int w = 0; w < 2; ++w) {
             const uint32_t dq = sbase + (w ? P_SM_QB : P_SM_QA);
             const int c1 = (int)row0, c2 = (int)(hA + w);
             if (maps.q_swap) {
-              tma_load_3d(dq, &maps.q, 0, c2, c1, bar(PB_Q));
-              tma_load_3d(dq + HALF, &maps.q, 64, c2, c1, bar(PB_Q));
+              tma_load_3d_if(lead, dq, &maps.q, 0, c2, c1, bar(PB_Q));
+              tma_load_3d_if(lead, dq + HALF, &maps.q, 64, c2, c1, bar(PB_Q));
             } else {
-              tma_load_3d(dq, &maps.q, 0, c1, c2, bar(PB_Q));
-              tma_load_3d(dq + HALF, &maps.q, 64, c1, c2, bar(PB_Q));
+              tma_load_3d_if(lead, dq, &maps.q, 0, c1, c2, bar(PB_Q));
+              tma_load_3d_if(lead, dq + HALF, &maps.q, 64, c1, c2, bar(PB_Q));
             }
           }
         }
@@ -833,16 +873,16 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
           const Tile2 tl = tile2_at(p, sc, t_begin + j);
           const uint32_t dst = sbase + P_SM_KV + (uint32_t)b * TILE;
           if (tl.kind == 0) {
-            if (lane == 0) {
+            {
               const CUtensorMap* m = is_v ? &maps.v : &maps.k;
               const int c1 = (int)tl.k0, c2 = (int)kvh;
-              mbar_expect_tx(bar(PB_FULL + b), TILE);
+              mbar_expect_tx_if(lead, bar(PB_FULL + b), TILE);
               if (maps.kv_swap) {
-                tma_load_3d(dst, m, 0, c2, c1, bar(PB_FULL + b));
-                tma_load_3d(dst + HALF, m, 64, c2, c1, bar(PB_FULL + b));
+                tma_load_3d_if(lead, dst, m, 0, c2, c1, bar(PB_FULL + b));
+                tma_load_3d_if(lead, dst + HALF, m, 64, c2, c1, bar(PB_FULL + b));
               } else {
-                tma_load_3d(dst, m, 0, c1, c2, bar(PB_FULL + b));
-                tma_load_3d(dst + HALF, m, 64, c1, c2, bar(PB_FULL + b));
+                tma_load_3d_if(lead, dst, m, 0, c1, c2, bar(PB_FULL + b));
+                tma_load_3d_if(lead, dst + HALF, m, 64, c1, c2, bar(PB_FULL + b));
               }
             }
           } else {
@@ -861,17 +901,18 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
             asm volatile("cp.async.wait_all;" ::: "memory");
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(PB_FULL + b));
+            mbar_arrive_if(lead, bar(PB_FULL + b));
           }
           ++fills[b];
         }
       }
-      if (lane == 0) {
+      {
         if (nt > 0) mbar_drain(bar(PB_Q), 0);
         for (int b = 0; b < PNB; ++b)
           if (fills[b] > 0) mbar_drain(bar(PB_FULL + b), (fills[b] - 1) & 1);
       }
-    } else if (warp == 1 && lane == 0 && nt > 0) {
+    } else if (warp == 1 && nt > 0) {
+      const uint32_t lead = lane == 0;
       // ---------------------------------------------------------------- MMA issuer
       constexpr uint32_t ID_QK = idesc<T>(false), ID_PV = idesc<T>(true);
       auto s_mma = [&](int w, uint32_t kb) {
@@ -879,9 +920,9 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t off = (uint32_t)(k >> 2) * HALF + (uint32_t)(k & 3) * 32u;
-          mma_ss(tmem + (uint32_t)w * 128u, desc_k(qs + off), desc_k(kb + off), ID_QK, k > 0 ? 1u : 0u);
+          mma_ss_if(lead, tmem + (uint32_t)w * 128u, desc_k(qs + off), desc_k(kb + off), ID_QK, k > 0 ? 1u : 0u);
         }
-        mma_commit(bar(PB_S + w));
+        mma_commit_if(lead, bar(PB_S + w));
       };
       // O_w += P_w(i) V_i; `wait_v`: the first of the two heads also waits for V_i to land.
       auto pv = [&](int w, int i, bool wait_v) -> bool {
@@ -892,9 +933,9 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
         const uint32_t vb = sbase + P_SM_KV + (uint32_t)bv * TILE;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          mma_ts(tmem + 256u + (uint32_t)w * 128u, tmem + (uint32_t)w * 128u + (uint32_t)k * 8u,
+          mma_ts_if(lead, tmem + 256u + (uint32_t)w * 128u, tmem + (uint32_t)w * 128u + (uint32_t)k * 8u,
                  desc_mn(vb + (uint32_t)k * 2048u), ID_PV, (i > 0 || k > 0) ? 1u : 0u);
-        mma_commit(bar(PB_O + w));
+        mma_commit_if(lead, bar(PB_O + w));
         return true;
       };
       bool ok = mbar_wait(bar(PB_Q), 0, abort_flag, F_MMA_Q);
@@ -910,17 +951,17 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
           if (!(ok = pv(0, j - 1, true))) break;
           s_mma(0, kb);
           if (!(ok = pv(1, j - 1, false))) break;
-          mma_commit(bar(PB_EMPTY + (2 * (j - 1) + 1) % PNB));  // V_{j-1} consumed by both heads
+          mma_commit_if(lead, bar(PB_EMPTY + (2 * (j - 1) + 1) % PNB));  // V_{j-1} consumed by both heads
           s_mma(1, kb);
         } else {
           s_mma(0, kb);
           s_mma(1, kb);
         }
-        mma_commit(bar(PB_EMPTY + bk));  // K_j consumed by both heads
+        mma_commit_if(lead, bar(PB_EMPTY + bk));  // K_j consumed by both heads
       }
       if (ok && pv(0, nt - 1, true) && pv(1, nt - 1, false))
-        mma_commit(bar(PB_EMPTY + (2 * (nt - 1) + 1) % PNB));
-      mma_commit(bar(PB_DONE));
+        mma_commit_if(lead, bar(PB_EMPTY + (2 * (nt - 1) + 1) % PNB));
+      mma_commit_if(lead, bar(PB_DONE));
       mbar_drain(bar(PB_DONE), 0);
     }
   } else {

@@ -52,11 +52,75 @@ __global__ void __launch_bounds__(256) rope_kernel(T* __restrict__ x, const T* _
   }
 }
 
+// 16-bit types, rows on 16-byte boundaries, D/2 a multiple of 8: each thread moves one 16-byte
+// vector of x from each half of a row (and the matching cos/sin vectors) with single loads and
+// stores. Same arithmetic as rope_kernel.
+template <typename T>
+__global__ void __launch_bounds__(256) rope_vec16_kernel(T* __restrict__ x, const T* __restrict__ cos,
+                                                         const T* __restrict__ sin, int64_t B, int64_t H,
+                                                         int64_t T_, int64_t D, int64_t sxb, int64_t sxh,
+                                                         int64_t sxt, int64_t scb, int64_t sct) {
+  using E = Elem<T>;
+  const int64_t half = D / 2;
+  const int64_t chunks = half / 8;
+  const int64_t total = B * H * T_ * chunks;
+  for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < total;
+       w += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = w % chunks;
+    int64_t r = w / chunks;
+    const int64_t t = r % T_;
+    r /= T_;
+    const int64_t h = r % H;
+    const int64_t b = r / H;
+    T* row = x + b * sxb + h * sxh + t * sxt + c * 8;
+    const T* cr = cos + b * scb + t * sct + c * 8;
+    const T* sr = sin + b * scb + t * sct + c * 8;
+    uint4 vx1 = *reinterpret_cast<const uint4*>(row);
+    uint4 vx2 = *reinterpret_cast<const uint4*>(row + half);
+    const uint4 vc1 = __ldg(reinterpret_cast<const uint4*>(cr));
+    const uint4 vc2 = __ldg(reinterpret_cast<const uint4*>(cr + half));
+    const uint4 vs1 = __ldg(reinterpret_cast<const uint4*>(sr));
+    const uint4 vs2 = __ldg(reinterpret_cast<const uint4*>(sr + half));
+    T* x1 = reinterpret_cast<T*>(&vx1);
+    T* x2 = reinterpret_cast<T*>(&vx2);
+    const T* c1 = reinterpret_cast<const T*>(&vc1);
+    const T* c2 = reinterpret_cast<const T*>(&vc2);
+    const T* s1 = reinterpret_cast<const T*>(&vs1);
+    const T* s2 = reinterpret_cast<const T*>(&vs2);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float a = E::to_f(x1[j]), bq = E::to_f(x2[j]);
+      const float lo = E::round(__fadd_rn(E::round(__fmul_rn(a, E::to_f(c1[j]))),
+                                          E::round(__fmul_rn(-bq, E::to_f(s1[j])))));
+      const float hi = E::round(__fadd_rn(E::round(__fmul_rn(bq, E::to_f(c2[j]))),
+                                          E::round(__fmul_rn(a, E::to_f(s2[j])))));
+      x1[j] = E::from_f(lo);
+      x2[j] = E::from_f(hi);
+    }
+    *reinterpret_cast<uint4*>(row) = vx1;
+    *reinterpret_cast<uint4*>(row + half) = vx2;
+  }
+}
+
 template <typename T>
 int launch_rope(void* x, int64_t B, int64_t H, int64_t T_, int64_t D, int64_t sxb, int64_t sxh,
                 int64_t sxt, const void* cos, const void* sin, int64_t scb, int64_t sct,
                 cudaStream_t stream) {
   const int64_t half = D / 2;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if constexpr (sizeof(T) == 2) {
+    if (half % 8 == 0 && al16(x) && al16(cos) && al16(sin) && (sxb * 2) % 16 == 0 && (sxh * 2) % 16 == 0 &&
+        (sxt * 2) % 16 == 0 && (scb * 2) % 16 == 0 && (sct * 2) % 16 == 0) {
+      const int64_t total = B * H * T_ * (half / 8);
+      if (total == 0) return BB_OK;
+      const int64_t grid = std::min<int64_t>(cdiv(total, 256), (int64_t)num_sms() * 16);
+      rope_vec16_kernel<T><<<grid, 256, 0, stream>>>(static_cast<T*>(x), static_cast<const T*>(cos),
+                                                      static_cast<const T*>(sin), B, H, T_, D, sxb, sxh, sxt,
+                                                      scb, sct);
+      BB_CHECK_LAUNCH("rope_vec16_kernel");
+      return BB_OK;
+    }
+  }
   const int vec = (half % 8 == 0) ? 8 : ((half % 4 == 0) ? 4 : 1);
   const int64_t total = B * H * T_ * (half / vec);
   if (total == 0) return BB_OK;

@@ -216,12 +216,12 @@ __global__ void __launch_bounds__(RT_THREADS, 2) route_stats_kernel(RtParams p) 
         float sum = 0.f;
         if (mnew != -INFINITY) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) sum += expf(s[i] - mnew);
+          for (int i = 0; i < 16; ++i) sum += __expf(s[i] - mnew);
         }
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
         if (mnew != -INFINITY) {
-          l[mt][h] = (m[mt][h] == -INFINITY ? 0.f : l[mt][h] * expf(m[mt][h] - mnew)) + sum;
+          l[mt][h] = (m[mt][h] == -INFINITY ? 0.f : l[mt][h] * __expf(m[mt][h] - mnew)) + sum;
           m[mt][h] = mnew;
         }
       }
@@ -261,8 +261,11 @@ __global__ void __launch_bounds__(RT_THREADS, 2) route_col_kernel(RtParams p) {
   rt_load_k<T, DP>(p, ks, kv, key_begin);
   cp_async_commit();
 
-  for (int row = threadIdx.x; row < RT_ROWS; row += RT_THREADS)
-    rowstat[row] = p.merged[((int64_t)kv * p.row_blocks + hb) * RT_ROWS + row];
+  for (int row = threadIdx.x; row < RT_ROWS; row += RT_THREADS) {
+    // (max, 1 / sum): p = exp(s - max) / sum is evaluated as exp(s - max) * (1 / sum).
+    const float2 ml = p.merged[((int64_t)kv * p.row_blocks + hb) * RT_ROWS + row];
+    rowstat[row] = make_float2(ml.x, ml.y > 0.f ? 1.f / ml.y : 0.f);
+  }
 
   for (int t = 0; t < tiles; ++t) {
     if (t + 1 < tiles) rt_load_k<T, DP>(p, ks + ((t + 1) & 1) * RT_BN * RtSmem<DP>::LD, kv,
@@ -289,7 +292,7 @@ __global__ void __launch_bounds__(RT_THREADS, 2) route_col_kernel(RtParams p) {
           for (int e = 0; e < 2; ++e) {
             const int64_t key = key0 + nt * 8 + (lane % 4) * 2 + e;
             const float s = rt_score<T>(acc[mt][nt][h * 2 + e], key, qp, p.n, p.scaling);
-            const float pr = (s == -INFINITY || st.y <= 0.f) ? 0.f : expf(s - st.x) / st.y;
+            const float pr = s == -INFINITY ? 0.f : __expf(s - st.x) * st.y;
             const int i = nt * 2 + e;
             pooled[i] = p.pool == BB_POOL_MAX ? fmaxf(pooled[i], pr) : pooled[i] + pr;
           }
