@@ -229,6 +229,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     from utmist_bigger_bird_b200 import _lib, _ops
+    from utmist_bigger_bird_b200.sharding import kv_head_shard, reduce_step
     from utmist_bigger_bird_b200.attention import route_query_positions, vertical_budget
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -240,10 +241,8 @@ def run_ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
     cfg = CONFIGS[args.config]
-    if cfg.kv_heads % world:
-        raise SystemExit(f"{cfg.kv_heads} KV heads do not split over {world} ranks")
-    per = cfg.kv_heads // world
-    kv_heads = list(range(rank * per, (rank + 1) * per))
+    kv_heads = kv_head_shard(rank, world, cfg.kv_heads)
+    per = len(kv_heads)
     g = cfg.heads // cfg.kv_heads
     H = per * g
     n, d = cfg.n, cfg.head_dim
@@ -281,15 +280,7 @@ def run_ours(args):
     # exact FLOPs of this rank's step from its routes (routes are input-determined: identical every step)
     pairs, _ = attended_pairs(n, cfg.sink, cfg.window, cfg.exact_tail, idx.cpu().numpy())
     flops = 4.0 * d * float(pairs)
-    t = torch.tensor([ms, flops], dtype=torch.float64, device=dev)
-    if world > 1:
-        tmax = t[:1].clone()
-        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-        fsum = t[1:].clone()
-        dist.all_reduce(fsum, op=dist.ReduceOp.SUM)
-        ms_max, flops_all = tmax.item(), fsum.item()
-    else:
-        ms_max, flops_all = ms, flops
+    ms_max, flops_all = reduce_step(ms, flops, dev)
     value = flops_all / (ms_max * 1e-3) / 1e12
 
     # ---- dominant kernel (main sparse pass) and routing, timed alone on this rank
@@ -354,10 +345,8 @@ def run_ours(args):
     e2e_ms = event_time(e2e_step, max(3, min(args.steps, 5)), stream)
     h2d = sum(t.numel() * t.element_size() for t in (q_h, k_h, v_h, cos_h, sin_h))
     d2h = out_h.numel() * out_h.element_size()
-    te = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = flops_all / (te.item() * 1e-3) / 1e12
+    e2e_max, _ = reduce_step(e2e_ms, 0.0, dev)
+    e2e_value = flops_all / (e2e_max * 1e-3) / 1e12
 
     # ---- CPU baseline (rank 0, N = 1 only)
     cpu = None
@@ -393,7 +382,7 @@ def run_ours(args):
         "exact_tail_ms": tail_ms,
         "dense_sdpa": {"ms": dense_ms, "speedup_sparse_vs_dense": dense_ms / ms},
         "cpu_baseline": cpu,
-        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms": te.item(), "h2d_bytes_per_step": h2d,
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms": e2e_max, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": int(launches),
         "clocks": clock,
