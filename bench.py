@@ -325,26 +325,59 @@ def run_ours(args):
     torch.cuda.synchronize(dev)
     dense_ms = event_time(dense, max(2, reps // 2), stream)
 
-    # ---- end to end through the C entry point with host buffers (H2D inputs, D2H output)
-    out_h = torch.empty((n, H, d), dtype=q.dtype).pin_memory()
-    qe, ke = torch.empty_like(q0), torch.empty_like(k0)
-
-    def e2e_step():
-        qe.copy_(q_h, non_blocking=True)
-        ke.copy_(k_h, non_blocking=True)
-        v.copy_(v_h, non_blocking=True)
-        cos.copy_(cos_h, non_blocking=True)
-        sin.copy_(sin_h, non_blocking=True)
-        _ops.sparse_prefill_(qe[0], ke[0], v[0], qpos, out, idx, sink=cfg.sink, window=cfg.window, budget=budget,
-                             exact_tail=cfg.exact_tail, scaling=cfg.scaling, cos=cos[0], sin=sin[0])
-        out_h.copy_(out.permute(1, 0, 2), non_blocking=True)
-
-    for _ in range(2):
-        e2e_step()
-    barrier()
-    e2e_ms = event_time(e2e_step, max(3, min(args.steps, 5)), stream)
+    # ---- end to end through the C entry point with host buffers: every step copies its q/k/v/cos/sin
+    # from pinned host memory and its output back. Steps are pipelined the way a serving loop runs
+    # them: two device buffer sets; H2D of step i+1 and D2H of step i-1 overlap the compute of step i
+    # (copy-in stream, compute stream, copy-out stream, ordered by events).
+    del qr, kr
+    torch.cuda.empty_cache()
     h2d = sum(t.numel() * t.element_size() for t in (q_h, k_h, v_h, cos_h, sin_h))
-    d2h = out_h.numel() * out_h.element_size()
+    out_h = [torch.empty((n, H, d), dtype=q.dtype).pin_memory() for _ in range(2)]
+    d2h = out_h[0].numel() * out_h[0].element_size()
+    bufs = [dict(q=torch.empty_like(q0), k=torch.empty_like(k0), v=torch.empty_like(v),
+                 cos=torch.empty_like(cos), sin=torch.empty_like(sin),
+                 out=torch.empty((n, H, d), device=dev, dtype=q.dtype).permute(1, 0, 2),
+                 idx=torch.empty((H, budget), device=dev, dtype=torch.int32)) for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    in_ready = [ev() for _ in range(2)]
+    computed = [ev() for _ in range(2)]
+    drained = [ev() for _ in range(2)]
+    inputs_free = [ev() for _ in range(2)]
+    for e in drained + inputs_free:
+        e.record(stream)
+
+    def e2e_run(steps):
+        for i in range(steps):
+            b = bufs[i % 2]
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(inputs_free[i % 2])
+                for name, src in (("q", q_h), ("k", k_h), ("v", v_h), ("cos", cos_h), ("sin", sin_h)):
+                    b[name].copy_(src, non_blocking=True)
+                in_ready[i % 2].record(s_in)
+            stream.wait_event(in_ready[i % 2])
+            stream.wait_event(drained[i % 2])
+            _ops.sparse_prefill_(b["q"][0], b["k"][0], b["v"][0], qpos, b["out"], b["idx"], sink=cfg.sink,
+                                 window=cfg.window, budget=budget, exact_tail=cfg.exact_tail, scaling=cfg.scaling,
+                                 cos=b["cos"][0], sin=b["sin"][0])
+            computed[i % 2].record(stream)
+            inputs_free[i % 2].record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(computed[i % 2])
+                out_h[i % 2].copy_(b["out"].permute(1, 0, 2), non_blocking=True)
+                drained[i % 2].record(s_out)
+
+    e2e_run(2)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_steps = max(3, min(args.steps, 5))
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record(s_in)
+    e2e_run(e2e_steps)
+    s_in.wait_stream(s_out)
+    t_end.record(s_in)
+    t_end.synchronize()
+    e2e_ms = t_start.elapsed_time(t_end) / e2e_steps
     e2e_max, _ = reduce_step(e2e_ms, 0.0, dev)
     e2e_value = flops_all / (e2e_max * 1e-3) / 1e12
 

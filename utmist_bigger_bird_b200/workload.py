@@ -96,6 +96,8 @@ def make_layer(cfg: LayerConfig, kv_heads=None, device="cpu"):
     g = cfg.heads // cfg.kv_heads
     kv_heads = list(range(cfg.kv_heads)) if kv_heads is None else list(kv_heads)
     hi = cfg.plant_hi if cfg.plant_hi is not None else n - cfg.window
+    if hi <= cfg.plant_lo:  # window covers the whole prompt: plant anywhere past the sink
+        hi = n
     cos32, sin32 = rope_tables(n, d, cfg.theta, torch.float32)
     q = torch.empty(1, g * len(kv_heads), n, d, dtype=cfg.dtype)
     k = torch.empty(1, len(kv_heads), n, d, dtype=cfg.dtype)
