@@ -88,9 +88,18 @@ __device__ __forceinline__ uint64_t gtimer() {
 }
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 
-// Waits for the phase of `parity`; false if another role aborted or ~2 s passed (then aborts).
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag, int code) {
-  if (mbar_try(bar, parity)) return true;
+// Waits for the phase of `parity`: false if another role aborted or ~2 s passed (then it aborts).
+// Fully inline (a call here costs the hand-offs on the critical path measurably): one
+// non-blocking test for the common already-completed case, then a try_wait spin that looks at
+// the abort flag and the clock every 64 polls.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag, int code) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  if (ok) return true;
   const uint64_t t0 = gtimer();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try(bar, parity)) return true;
@@ -103,6 +112,14 @@ __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile u
       }
     }
   }
+}
+// mbar_wait for the single-warp roles (producer, MMA issuer): every lane polls, and the result is
+// made warp-uniform (false if any lane gave up), so the warp stays converged for the elect.sync
+// issue that follows and all lanes leave together on an abort.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                               int code) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, code);
+  return __all_sync(0xffffffffu, ok);
 }
 // Bounded wait used while draining on the way out (ignores the abort flag).
 __device__ __noinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
@@ -119,22 +136,23 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// Issue-side wrappers for a converged warp: every lane executes the instruction with operands the
-// compiler can keep in uniform registers, and only the lane with `lead` != 0 (predicate) issues.
-__device__ __forceinline__ void mbar_expect_tx_if(uint32_t lead, uint32_t bar, uint32_t bytes) {
-  asm volatile("{\n .reg .pred q;\n setp.ne.b32 q, %2, 0;\n @q mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n}\n"
-               ::"r"(bar), "r"(bytes), "r"(lead) : "memory");
+// Issue-side wrappers for a converged warp: all 32 lanes execute the block, elect.sync picks the
+// one lane that issues. Measured on this kernel, an elected issue keeps the tensor pipe fed
+// noticeably better than the same instructions predicated on a lane-index register.
+__device__ __forceinline__ void mbar_expect_tx_one(uint32_t bar, uint32_t bytes) {
+  asm volatile("{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n @e mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n}\n"
+               ::"r"(bar), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ void mbar_arrive_if(uint32_t lead, uint32_t bar) {
-  asm volatile("{\n .reg .pred q;\n setp.ne.b32 q, %1, 0;\n @q mbarrier.arrive.shared::cta.b64 _, [%0];\n}\n"
-               ::"r"(bar), "r"(lead) : "memory");
+__device__ __forceinline__ void mbar_arrive_one(uint32_t bar) {
+  asm volatile("{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n @e mbarrier.arrive.shared::cta.b64 _, [%0];\n}\n"
+               ::"r"(bar) : "memory");
 }
-__device__ __forceinline__ void tma_load_3d_if(uint32_t lead, uint32_t dst, const CUtensorMap* map, int c0, int c1,
-                                               int c2, uint32_t bar) {
+__device__ __forceinline__ void tma_load_3d_one(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                                uint32_t bar) {
   asm volatile(
-      "{\n .reg .pred q;\n setp.ne.b32 q, %6, 0;\n"
-      " @q cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n}\n"
-      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar), "r"(lead)
+      "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+      " @e cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n}\n"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
       : "memory");
 }
 
@@ -162,37 +180,56 @@ template <typename T> __host__ __device__ constexpr uint32_t idesc(bool b_mn) {
          ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-      ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
-}
-__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
-      ::"r"(d), "r"(a_tmem), "l"(b), "r"(id), "r"(acc));
-}
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-               : "memory");
+__device__ __forceinline__ void mma_commit_one(uint32_t bar) {
+  asm volatile("{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+               " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n"
+               ::"r"(bar) : "memory");
 }
 
-__device__ __forceinline__ void mma_ss_if(uint32_t lead, uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+// A whole 128x128x128 GEMM (8 K-steps of 16) in one asm block, issued by one elected lane of a
+// converged warp: the predicates are set once and every descriptor is formed before the first
+// MMA, so the eight tcgen05.mma issue back to back.
+// The issuing warp shares its SM sub-partition with two busy softmax warps; with one small asm
+// block per step the instructions between steps lose issue slots and the tensor pipe drains.
+// S = Q K^T, both operands K-major SW128: a K-step advances the start address by 32 B (+2 in
+// descriptor units) inside the 128 B row and by a 16 KB half tile (+1024) after four steps.
+__device__ __forceinline__ void gemm_ss8(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
   asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.b32 p, %4, 0;\n setp.ne.b32 q, %5, 0;\n"
-      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-      ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc), "r"(lead));
+      "{\n .reg .pred q, p, t;\n .reg .b64 a1, a2, a3, a4, a5, a6, a7, b1, b2, b3, b4, b5, b6, b7;\n"
+      " elect.sync _|q, 0xffffffff;\n setp.ne.b32 p, %4, 0;\n setp.eq.b32 t, %4, %4;\n"
+      " add.s64 a1, %1, 2;\n add.s64 a2, %1, 4;\n add.s64 a3, %1, 6;\n add.s64 a4, %1, 1024;\n"
+      " add.s64 a5, %1, 1026;\n add.s64 a6, %1, 1028;\n add.s64 a7, %1, 1030;\n"
+      " add.s64 b1, %2, 2;\n add.s64 b2, %2, 4;\n add.s64 b3, %2, 6;\n add.s64 b4, %2, 1024;\n"
+      " add.s64 b5, %2, 1026;\n add.s64 b6, %2, 1028;\n add.s64 b7, %2, 1030;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, t;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, t;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, t;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], a4, b4, %3, t;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], a5, b5, %3, t;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], a6, b6, %3, t;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], a7, b7, %3, t;\n}\n"
+      ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
 }
-__device__ __forceinline__ void mma_ts_if(uint32_t lead, uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t acc) {
+// O += P V: P (A) from TMEM, 8 columns (16 packed keys) per K-step; V (B) MN-major SW128, 16 key
+// rows = 2048 B (+128 in descriptor units) per K-step.
+__device__ __forceinline__ void gemm_ts8(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t acc) {
   asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.b32 p, %4, 0;\n setp.ne.b32 q, %5, 0;\n"
-      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
-      ::"r"(d), "r"(a_tmem), "l"(b), "r"(id), "r"(acc), "r"(lead));
-}
-__device__ __forceinline__ void mma_commit_if(uint32_t lead, uint32_t bar) {
-  asm volatile("{\n .reg .pred q;\n setp.ne.b32 q, %1, 0;\n"
-               " @q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n"
-               ::"r"(bar), "r"(lead) : "memory");
+      "{\n .reg .pred q, p, t;\n .reg .b32 t1, t2, t3, t4, t5, t6, t7;\n .reg .b64 b1, b2, b3, b4, b5, b6, b7;\n"
+      " elect.sync _|q, 0xffffffff;\n setp.ne.b32 p, %4, 0;\n setp.eq.b32 t, %4, %4;\n"
+      " add.u32 t1, %1, 8;\n add.u32 t2, %1, 16;\n add.u32 t3, %1, 24;\n add.u32 t4, %1, 32;\n"
+      " add.u32 t5, %1, 40;\n add.u32 t6, %1, 48;\n add.u32 t7, %1, 56;\n"
+      " add.s64 b1, %2, 128;\n add.s64 b2, %2, 256;\n add.s64 b3, %2, 384;\n add.s64 b4, %2, 512;\n"
+      " add.s64 b5, %2, 640;\n add.s64 b6, %2, 768;\n add.s64 b7, %2, 896;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [t1], b1, %3, t;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [t2], b2, %3, t;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [t3], b3, %3, t;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [t4], b4, %3, t;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [t5], b5, %3, t;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [t6], b6, %3, t;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [t7], b7, %3, t;\n}\n"
+      ::"r"(d), "r"(a_tmem), "l"(b), "r"(id), "r"(acc));
 }
 
 // 32 lanes x 32 consecutive 32-bit columns -> 32 registers per thread (load and wait together,
@@ -413,20 +450,23 @@ __device__ __forceinline__ MaskLimits mask_limits(int kind, int64_t k0, int64_t 
   }
   return m;
 }
-// Masks columns 64*half .. 64*half+63 of a row held in s[0..63].
-__device__ __forceinline__ void mask_half(float* s, int half, int kind, const MaskLimits& m, const int32_t* ps_s) {
-  const int base = 64 * half;
+// Masks columns base .. base+NC-1 of a row held in s[0..NC-1].
+template <int NC>
+__device__ __forceinline__ void mask_cols(float* s, int base, int kind, const MaskLimits& m, const int32_t* ps_s) {
   if (kind == 0) {
 #pragma unroll
-    for (int i = 0; i < 64; ++i)
+    for (int i = 0; i < NC; ++i)
       if (!(base + i <= m.hi && (base + i < m.f || base + i >= m.lo))) s[i] = -INFINITY;
   } else {
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
+    for (int i = 0; i < NC; ++i) {
       const int ps = ps_s[base + i];
       if (!(ps >= m.f && ps <= m.hi)) s[i] = -INFINITY;
     }
   }
+}
+__device__ __forceinline__ void mask_half(float* s, int half, int kind, const MaskLimits& m, const int32_t* ps_s) {
+  mask_cols<64>(s, 64 * half, kind, m, ps_s);
 }
 
 struct TcMaps {
@@ -484,7 +524,6 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
-    const uint32_t lead = lane == 0;
     int fills[NB];
 #pragma unroll
     for (int i = 0; i < NB; ++i) fills[i] = 0;
@@ -492,13 +531,13 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
     if (nt > 0) {
       {
         const int qc1 = (int)row0, qc2 = (int)h;
-        mbar_expect_tx_if(lead, bar(B_Q), TILE);
+        mbar_expect_tx_one(bar(B_Q), TILE);
         if (maps.q_swap) {
-          tma_load_3d_if(lead, sbase + SM_Q, &maps.q, 0, qc2, qc1, bar(B_Q));
-          tma_load_3d_if(lead, sbase + SM_Q + HALF, &maps.q, 64, qc2, qc1, bar(B_Q));
+          tma_load_3d_one(sbase + SM_Q, &maps.q, 0, qc2, qc1, bar(B_Q));
+          tma_load_3d_one(sbase + SM_Q + HALF, &maps.q, 64, qc2, qc1, bar(B_Q));
         } else {
-          tma_load_3d_if(lead, sbase + SM_Q, &maps.q, 0, qc1, qc2, bar(B_Q));
-          tma_load_3d_if(lead, sbase + SM_Q + HALF, &maps.q, 64, qc1, qc2, bar(B_Q));
+          tma_load_3d_one(sbase + SM_Q, &maps.q, 0, qc1, qc2, bar(B_Q));
+          tma_load_3d_one(sbase + SM_Q + HALF, &maps.q, 64, qc1, qc2, bar(B_Q));
         }
       }
       q_issued = true;
@@ -509,20 +548,20 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         const bool is_v = it & 1;
         const int b = it % NB;
         const int round = it / NB;
-        if (round > 0 && !mbar_wait(bar(B_EMPTY + b), (round - 1) & 1, abort_flag, F_PROD_EMPTY)) break;
+        if (round > 0 && !mbar_wait_warp(bar(B_EMPTY + b), (round - 1) & 1, abort_flag, F_PROD_EMPTY)) break;
         const Tile tl = tile_at(p, sc, t_begin + j);
         const uint32_t dst = sbase + SM_KV + (uint32_t)b * TILE;
         if (tl.kind == 0) {
           {
             const CUtensorMap* m = is_v ? &maps.v : &maps.k;
             const int c1 = (int)tl.k0, c2 = (int)kvh;
-            mbar_expect_tx_if(lead, bar(B_FULL + b), TILE);
+            mbar_expect_tx_one(bar(B_FULL + b), TILE);
             if (maps.kv_swap) {
-              tma_load_3d_if(lead, dst, m, 0, c2, c1, bar(B_FULL + b));
-              tma_load_3d_if(lead, dst + HALF, m, 64, c2, c1, bar(B_FULL + b));
+              tma_load_3d_one(dst, m, 0, c2, c1, bar(B_FULL + b));
+              tma_load_3d_one(dst + HALF, m, 64, c2, c1, bar(B_FULL + b));
             } else {
-              tma_load_3d_if(lead, dst, m, 0, c1, c2, bar(B_FULL + b));
-              tma_load_3d_if(lead, dst + HALF, m, 64, c1, c2, bar(B_FULL + b));
+              tma_load_3d_one(dst, m, 0, c1, c2, bar(B_FULL + b));
+              tma_load_3d_one(dst + HALF, m, 64, c1, c2, bar(B_FULL + b));
             }
           }
         } else {
@@ -542,7 +581,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
           asm volatile("cp.async.wait_all;" ::: "memory");
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
-          mbar_arrive_if(lead, bar(B_FULL + b));
+          mbar_arrive_one(bar(B_FULL + b));
         }
         ++fills[b];
       }
@@ -556,43 +595,35 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (nt > 0) {
-      const uint32_t lead = lane == 0;
       constexpr uint32_t ID_QK = idesc<T>(false), ID_PV = idesc<T>(true);
-      bool ok = mbar_wait(bar(B_Q), 0, abort_flag, F_MMA_Q);
+      bool ok = mbar_wait_warp(bar(B_Q), 0, abort_flag, F_MMA_Q);
       auto issue_pv = [&](int i) -> bool {
-        if (!mbar_wait(bar(B_P + (i & 1)), (i >> 1) & 1, abort_flag, F_MMA_P)) return false;
+        if (!mbar_wait_warp(bar(B_P + (i & 1)), (i >> 1) & 1, abort_flag, F_MMA_P)) return false;
         const int itv = 2 * i + 1, bv = itv % NB;
-        if (!mbar_wait(bar(B_FULL + bv), (itv / NB) & 1, abort_flag, F_MMA_V)) return false;
+        if (!mbar_wait_warp(bar(B_FULL + bv), (itv / NB) & 1, abort_flag, F_MMA_V)) return false;
         tc_fence_after();
         const uint32_t vb = sbase + SM_KV + (uint32_t)bv * TILE;
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          mma_ts_if(lead, tmem + COL_O, tmem + (uint32_t)(i & 1) * 128u + (uint32_t)k * 8u, desc_mn(vb + (uint32_t)k * 2048u),
-                 ID_PV, (i > 0 || k > 0) ? 1u : 0u);
-        mma_commit_if(lead, bar(B_O));
-        mma_commit_if(lead, bar(B_EMPTY + bv));
+        gemm_ts8(tmem + COL_O, tmem + (uint32_t)(i & 1) * 128u, desc_mn(vb), ID_PV, i > 0 ? 1u : 0u);
+        mma_commit_one(bar(B_O));
+        mma_commit_one(bar(B_EMPTY + bv));
         return true;
       };
       for (int j = 0; ok && j < nt; ++j) {
         const int itk = 2 * j, bk = itk % NB;
-        if (!mbar_wait(bar(B_FULL + bk), (itk / NB) & 1, abort_flag, F_MMA_K)) {
+        if (!mbar_wait_warp(bar(B_FULL + bk), (itk / NB) & 1, abort_flag, F_MMA_K)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t kb = sbase + SM_KV + (uint32_t)bk * TILE;
         const uint32_t ds = tmem + (uint32_t)(j & 1) * 128u;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t off = (uint32_t)(k >> 2) * HALF + (uint32_t)(k & 3) * 32u;
-          mma_ss_if(lead, ds, desc_k(sbase + SM_Q + off), desc_k(kb + off), ID_QK, k > 0 ? 1u : 0u);
-        }
-        mma_commit_if(lead, bar(B_S + (j & 1)));
-        mma_commit_if(lead, bar(B_EMPTY + bk));
+        gemm_ss8(ds, desc_k(sbase + SM_Q), desc_k(kb), ID_QK, 0u);
+        mma_commit_one(bar(B_S + (j & 1)));
+        mma_commit_one(bar(B_EMPTY + bk));
         if (j > 0) ok = issue_pv(j - 1);
       }
       if (ok) issue_pv(nt - 1);
-      mma_commit_if(lead, bar(B_DONE));
+      mma_commit_one(bar(B_DONE));
       mbar_drain(bar(B_DONE), 0);
     }
   } else {
@@ -749,7 +780,9 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
 // softmax of head A (warps 2-5) and of head B (warps 6-9); warp w reads TMEM lanes
 // 32 * (w % 4) .. 32 * (w % 4) + 31, so each softmax group covers all 128 rows.
 constexpr int P_THREADS = 320;
-constexpr int PNB = 4;
+// K/V ring: 5 slots of 32 KB (K_j, V_j alternate), the most that fits beside the two Q tiles in
+// 227 KB; the extra slot gives the TMA of the next tiles more lead over the MMA issuer.
+constexpr int PNB = 5;
 constexpr uint32_t P_SM_QA = 0;
 constexpr uint32_t P_SM_QB = TILE;
 constexpr uint32_t P_SM_KV = 2 * TILE;
@@ -759,6 +792,7 @@ enum { PB_Q = 0, PB_FULL = 1, PB_EMPTY = PB_FULL + PNB, PB_S = PB_EMPTY + PNB, P
 constexpr uint32_t P_SM_BAR = P_SM_POS + 2 * 128 * 4;
 constexpr uint32_t P_SM_MISC = P_SM_BAR + PN_BARS * 8;
 constexpr uint32_t P_SM_ALLOC = P_SM_MISC + 16 + 1024;
+static_assert(P_SM_ALLOC <= 232448, "pair kernel shared memory exceeds the 227 KB per-block limit");
 
 struct Tile2 {
   int kind;   // 0 contiguous (both heads), 1 routed
@@ -843,22 +877,21 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
   if (warp < 2) {
     if (warp == 0) {
       // ---------------------------------------------------------------- producer
-      const uint32_t lead = lane == 0;
       int fills[PNB];
 #pragma unroll
       for (int i = 0; i < PNB; ++i) fills[i] = 0;
       if (nt > 0) {
         {
-          mbar_expect_tx_if(lead, bar(PB_Q), 2 * TILE);
+          mbar_expect_tx_one(bar(PB_Q), 2 * TILE);
           for (int w = 0; w < 2; ++w) {
             const uint32_t dq = sbase + (w ? P_SM_QB : P_SM_QA);
             const int c1 = (int)row0, c2 = (int)(hA + w);
             if (maps.q_swap) {
-              tma_load_3d_if(lead, dq, &maps.q, 0, c2, c1, bar(PB_Q));
-              tma_load_3d_if(lead, dq + HALF, &maps.q, 64, c2, c1, bar(PB_Q));
+              tma_load_3d_one(dq, &maps.q, 0, c2, c1, bar(PB_Q));
+              tma_load_3d_one(dq + HALF, &maps.q, 64, c2, c1, bar(PB_Q));
             } else {
-              tma_load_3d_if(lead, dq, &maps.q, 0, c1, c2, bar(PB_Q));
-              tma_load_3d_if(lead, dq + HALF, &maps.q, 64, c1, c2, bar(PB_Q));
+              tma_load_3d_one(dq, &maps.q, 0, c1, c2, bar(PB_Q));
+              tma_load_3d_one(dq + HALF, &maps.q, 64, c1, c2, bar(PB_Q));
             }
           }
         }
@@ -869,20 +902,20 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
           const bool is_v = it & 1;
           const int b = it % PNB;
           const int round = it / PNB;
-          if (round > 0 && !mbar_wait(bar(PB_EMPTY + b), (round - 1) & 1, abort_flag, F_PROD_EMPTY)) break;
+          if (round > 0 && !mbar_wait_warp(bar(PB_EMPTY + b), (round - 1) & 1, abort_flag, F_PROD_EMPTY)) break;
           const Tile2 tl = tile2_at(p, sc, t_begin + j);
           const uint32_t dst = sbase + P_SM_KV + (uint32_t)b * TILE;
           if (tl.kind == 0) {
             {
               const CUtensorMap* m = is_v ? &maps.v : &maps.k;
               const int c1 = (int)tl.k0, c2 = (int)kvh;
-              mbar_expect_tx_if(lead, bar(PB_FULL + b), TILE);
+              mbar_expect_tx_one(bar(PB_FULL + b), TILE);
               if (maps.kv_swap) {
-                tma_load_3d_if(lead, dst, m, 0, c2, c1, bar(PB_FULL + b));
-                tma_load_3d_if(lead, dst + HALF, m, 64, c2, c1, bar(PB_FULL + b));
+                tma_load_3d_one(dst, m, 0, c2, c1, bar(PB_FULL + b));
+                tma_load_3d_one(dst + HALF, m, 64, c2, c1, bar(PB_FULL + b));
               } else {
-                tma_load_3d_if(lead, dst, m, 0, c1, c2, bar(PB_FULL + b));
-                tma_load_3d_if(lead, dst + HALF, m, 64, c1, c2, bar(PB_FULL + b));
+                tma_load_3d_one(dst, m, 0, c1, c2, bar(PB_FULL + b));
+                tma_load_3d_one(dst + HALF, m, 64, c1, c2, bar(PB_FULL + b));
               }
             }
           } else {
@@ -901,7 +934,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
             asm volatile("cp.async.wait_all;" ::: "memory");
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
-            mbar_arrive_if(lead, bar(PB_FULL + b));
+            mbar_arrive_one(bar(PB_FULL + b));
           }
           ++fills[b];
         }
@@ -912,36 +945,28 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
           if (fills[b] > 0) mbar_drain(bar(PB_FULL + b), (fills[b] - 1) & 1);
       }
     } else if (warp == 1 && nt > 0) {
-      const uint32_t lead = lane == 0;
       // ---------------------------------------------------------------- MMA issuer
       constexpr uint32_t ID_QK = idesc<T>(false), ID_PV = idesc<T>(true);
       auto s_mma = [&](int w, uint32_t kb) {
         const uint32_t qs = sbase + (w ? P_SM_QB : P_SM_QA);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t off = (uint32_t)(k >> 2) * HALF + (uint32_t)(k & 3) * 32u;
-          mma_ss_if(lead, tmem + (uint32_t)w * 128u, desc_k(qs + off), desc_k(kb + off), ID_QK, k > 0 ? 1u : 0u);
-        }
-        mma_commit_if(lead, bar(PB_S + w));
+        gemm_ss8(tmem + (uint32_t)w * 128u, desc_k(qs), desc_k(kb), ID_QK, 0u);
+        mma_commit_one(bar(PB_S + w));
       };
       // O_w += P_w(i) V_i; `wait_v`: the first of the two heads also waits for V_i to land.
       auto pv = [&](int w, int i, bool wait_v) -> bool {
-        if (!mbar_wait(bar(PB_P + w), i & 1, abort_flag, F_MMA_P)) return false;
+        if (!mbar_wait_warp(bar(PB_P + w), i & 1, abort_flag, F_MMA_P)) return false;
         const int itv = 2 * i + 1, bv = itv % PNB;
-        if (wait_v && !mbar_wait(bar(PB_FULL + bv), (itv / PNB) & 1, abort_flag, F_MMA_V)) return false;
+        if (wait_v && !mbar_wait_warp(bar(PB_FULL + bv), (itv / PNB) & 1, abort_flag, F_MMA_V)) return false;
         tc_fence_after();
         const uint32_t vb = sbase + P_SM_KV + (uint32_t)bv * TILE;
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          mma_ts_if(lead, tmem + 256u + (uint32_t)w * 128u, tmem + (uint32_t)w * 128u + (uint32_t)k * 8u,
-                 desc_mn(vb + (uint32_t)k * 2048u), ID_PV, (i > 0 || k > 0) ? 1u : 0u);
-        mma_commit_if(lead, bar(PB_O + w));
+        gemm_ts8(tmem + 256u + (uint32_t)w * 128u, tmem + (uint32_t)w * 128u, desc_mn(vb), ID_PV, i > 0 ? 1u : 0u);
+        mma_commit_one(bar(PB_O + w));
         return true;
       };
-      bool ok = mbar_wait(bar(PB_Q), 0, abort_flag, F_MMA_Q);
+      bool ok = mbar_wait_warp(bar(PB_Q), 0, abort_flag, F_MMA_Q);
       for (int j = 0; ok && j < nt; ++j) {
         const int itk = 2 * j, bk = itk % PNB;
-        if (!mbar_wait(bar(PB_FULL + bk), (itk / PNB) & 1, abort_flag, F_MMA_K)) {
+        if (!mbar_wait_warp(bar(PB_FULL + bk), (itk / PNB) & 1, abort_flag, F_MMA_K)) {
           ok = false;
           break;
         }
@@ -951,17 +976,17 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
           if (!(ok = pv(0, j - 1, true))) break;
           s_mma(0, kb);
           if (!(ok = pv(1, j - 1, false))) break;
-          mma_commit_if(lead, bar(PB_EMPTY + (2 * (j - 1) + 1) % PNB));  // V_{j-1} consumed by both heads
+          mma_commit_one(bar(PB_EMPTY + (2 * (j - 1) + 1) % PNB));  // V_{j-1} consumed by both heads
           s_mma(1, kb);
         } else {
           s_mma(0, kb);
           s_mma(1, kb);
         }
-        mma_commit_if(lead, bar(PB_EMPTY + bk));  // K_j consumed by both heads
+        mma_commit_one(bar(PB_EMPTY + bk));  // K_j consumed by both heads
       }
       if (ok && pv(0, nt - 1, true) && pv(1, nt - 1, false))
-        mma_commit_if(lead, bar(PB_EMPTY + (2 * (nt - 1) + 1) % PNB));
-      mma_commit_if(lead, bar(PB_DONE));
+        mma_commit_one(bar(PB_EMPTY + (2 * (nt - 1) + 1) % PNB));
+      mma_commit_one(bar(PB_DONE));
       mbar_drain(bar(PB_DONE), 0);
     }
   } else {
@@ -998,11 +1023,44 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
         break;
       }
       tc_fence_after();
-      if (own) {
+      bool done = !own;
+      const MaskLimits ml = (own && tl.masked) ? mask_limits(tl.kind, tl.k0, tl.group, p, qpos, qgroup)
+                                               : MaskLimits{127, 128, 0};
+      if (own && m_ref > -1.0e20f) {
+        // Single pass against the current reference max: P = exp2(s * c - m_ref) is formed for
+        // all 128 columns (held packed in registers) while the tile max is found. It is stored
+        // when the tile max does not pass the reference by more than 2^RESCALE_LOG2, which is
+        // exactly the case in which the two-pass path below keeps m_ref, so both paths produce
+        // the same bits (same products, same summation order). S is untouched until then.
+        uint32_t pk[64];
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
+        const float neg = -m_ref;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float s[32];
+          tmem_ld32(scol + 32u * q, s);
+          if (tl.masked) mask_cols<32>(s, 32 * q, tl.kind, ml, ps_s);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            mx4[i & 3] = fmaxf(mx4[i & 3], fmaxf(s[2 * i], s[2 * i + 1]));
+            const float a = fast_exp2(fmaf(s[2 * i], c, neg));
+            const float b = fast_exp2(fmaf(s[2 * i + 1], c, neg));
+            ls[i & 3] += a + b;
+            pk[16 * q + i] = pack2<T>(a, b);
+          }
+        }
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+        if (!(mx * c > m_ref + RESCALE_LOG2)) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) tmem_st16(scol + 16u * q, pk + 16 * q);
+          l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+          done = true;
+        }
+      }
+      if (!done) {
         // Pass 1: row max over the two 64-column halves of S (re-read in pass 2, so only 64
-        // scores are live at a time and the softmax fits the 168-register budget).
-        const MaskLimits ml = tl.masked ? mask_limits(tl.kind, tl.k0, tl.group, p, qpos, qgroup)
-                                        : MaskLimits{127, 128, 0};
+        // scores are live at a time).
         float mx8[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
@@ -1058,7 +1116,8 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
           }
         }
         l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      } else {
+      }
+      if (!own) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) pk[i] = 0u;
