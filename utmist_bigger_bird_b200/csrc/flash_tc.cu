@@ -113,9 +113,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
   }
 }
-// mbar_wait for the single-warp roles (producer, MMA issuer): every lane polls, and the result is
-// made warp-uniform (false if any lane gave up), so the warp stays converged for the elect.sync
-// issue that follows and all lanes leave together on an abort.
+// mbar_wait made warp-uniform (false if any lane gave up): every lane polls, and the warp stays
+// converged for the elect.sync issue or the warp-wide (.sync.aligned) TMEM accesses that follow,
+// and leaves together on an abort.
 __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
                                                int code) {
   const bool ok = mbar_wait(bar, parity, abort_flag, code);
@@ -229,6 +229,19 @@ __device__ __forceinline__ void gemm_ts8(uint32_t d, uint32_t a_tmem, uint64_t b
       " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [t5], b5, %3, t;\n"
       " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [t6], b6, %3, t;\n"
       " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [t7], b7, %3, t;\n}\n"
+      ::"r"(d), "r"(a_tmem), "l"(b), "r"(id), "r"(acc));
+}
+// Half of the P.V GEMM: 4 K-steps (64 keys) starting at P column a_tmem and V descriptor b.
+__device__ __forceinline__ void gemm_ts4(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred q, p, t;\n .reg .b32 t1, t2, t3;\n .reg .b64 b1, b2, b3;\n"
+      " elect.sync _|q, 0xffffffff;\n setp.ne.b32 p, %4, 0;\n setp.eq.b32 t, %4, %4;\n"
+      " add.u32 t1, %1, 8;\n add.u32 t2, %1, 16;\n add.u32 t3, %1, 24;\n"
+      " add.s64 b1, %2, 128;\n add.s64 b2, %2, 256;\n add.s64 b3, %2, 384;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [t1], b1, %3, t;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [t2], b2, %3, t;\n"
+      " @q tcgen05.mma.cta_group::1.kind::f16 [%0], [t3], b3, %3, t;\n}\n"
       ::"r"(d), "r"(a_tmem), "l"(b), "r"(id), "r"(acc));
 }
 
@@ -643,7 +656,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         ps_s[row] = (int32_t)routed_pos(p, h, tl.group, tl.slot0 + row);
         named_sync(1, 128);
       }
-      if (!mbar_wait(bar(B_S + (j & 1)), (j >> 1) & 1, abort_flag, F_SOFTMAX_S)) {
+      if (!mbar_wait_warp(bar(B_S + (j & 1)), (j >> 1) & 1, abort_flag, F_SOFTMAX_S)) {
         ok = false;
         break;
       }
@@ -666,29 +679,35 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
       // The wait for P_{j-1} V_{j-1} (completion j of B_O) is taken in order every tile: here when
       // O must be rescaled, otherwise after the exponentials, by when it has normally completed.
       bool o_waited = j == 0;
+      float alpha = 1.f;
+      bool rescale_o = false;
       if (mt > m_ref + RESCALE_LOG2) {
-        const float alpha = fast_exp2(m_ref - mt);
+        alpha = fast_exp2(m_ref - mt);
+        rescale_o = j > 0 && m_ref > -1.0e20f;
+        l *= alpha;
+        m_ref = mt;
+      }
+      // The O rescale uses warp-wide TMEM loads/stores, so it is decided per warp: lanes that
+      // keep their reference multiply by exactly 1.
+      if (!rescale_o) alpha = 1.f;
+      if (__any_sync(0xffffffffu, rescale_o)) {
         if (!o_waited) {
-          if (!mbar_wait(bar(B_O), (j - 1) & 1, abort_flag, F_SOFTMAX_O)) {
+          if (!mbar_wait_warp(bar(B_O), (j - 1) & 1, abort_flag, F_SOFTMAX_O)) {
             ok = false;
             break;
           }
           o_waited = true;
         }
-        if (j > 0 && m_ref > -1.0e20f) {
-          tc_fence_after();
+        tc_fence_after();
 #pragma unroll 1
-          for (int q4 = 0; q4 < 4; ++q4) {
-            float o[32];
-            tmem_ld32(tl_lane + COL_O + q4 * 32, o);
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float o[32];
+          tmem_ld32(tl_lane + COL_O + q4 * 32, o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(tl_lane + COL_O + q4 * 32, o);
-          }
-          tmem_wait_st();
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(tl_lane + COL_O + q4 * 32, o);
         }
-        l *= alpha;
-        m_ref = mt;
+        tmem_wait_st();
       }
       uint32_t pk[64];
       float ls[4] = {0.f, 0.f, 0.f, 0.f};
@@ -701,7 +720,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         pk[i] = pack2<T>(a, b);
       }
       l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      if (!o_waited && !mbar_wait(bar(B_O), (j - 1) & 1, abort_flag, F_SOFTMAX_O)) {
+      if (!o_waited && !mbar_wait_warp(bar(B_O), (j - 1) & 1, abort_flag, F_SOFTMAX_O)) {
         ok = false;
         break;
       }
@@ -713,7 +732,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
     }
     // Epilogue: wait for the last P.V, normalise, store.
     bool have_o = false;
-    if (ok && nt > 0) have_o = mbar_wait(bar(B_O), (nt - 1) & 1, abort_flag, F_EPI_O);
+    if (ok && nt > 0) have_o = mbar_wait_warp(bar(B_O), (nt - 1) & 1, abort_flag, F_EPI_O);
     tc_fence_after();
     const int64_t lrow = row0 + row;
     const bool store = lrow < row1;
@@ -787,7 +806,8 @@ constexpr uint32_t P_SM_QA = 0;
 constexpr uint32_t P_SM_QB = TILE;
 constexpr uint32_t P_SM_KV = 2 * TILE;
 constexpr uint32_t P_SM_POS = P_SM_KV + PNB * TILE;  // [2 heads][128] int32 routed positions
-enum { PB_Q = 0, PB_FULL = 1, PB_EMPTY = PB_FULL + PNB, PB_S = PB_EMPTY + PNB, PB_P = PB_S + 2, PB_O = PB_P + 2,
+// PB_P + 2w: P_w columns for keys 0-63 stored, PB_P + 2w + 1: keys 64-127 stored.
+enum { PB_Q = 0, PB_FULL = 1, PB_EMPTY = PB_FULL + PNB, PB_S = PB_EMPTY + PNB, PB_P = PB_S + 2, PB_O = PB_P + 4,
        PB_DONE = PB_O + 2, PN_BARS = PB_DONE + 1 };
 constexpr uint32_t P_SM_BAR = P_SM_POS + 2 * 128 * 4;
 constexpr uint32_t P_SM_MISC = P_SM_BAR + PN_BARS * 8;
@@ -856,7 +876,8 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(PB_S + i), 1);
-      mbar_init(bar(PB_P + i), 128);
+      mbar_init(bar(PB_P + 2 * i), 128);
+      mbar_init(bar(PB_P + 2 * i + 1), 128);
       mbar_init(bar(PB_O + i), 1);
     }
     mbar_init(bar(PB_DONE), 1);
@@ -952,14 +973,19 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
         gemm_ss8(tmem + (uint32_t)w * 128u, desc_k(qs), desc_k(kb), ID_QK, 0u);
         mma_commit_one(bar(PB_S + w));
       };
-      // O_w += P_w(i) V_i; `wait_v`: the first of the two heads also waits for V_i to land.
+      // O_w += P_w(i) V_i in two K halves (keys 0-63, 64-127), each issued as soon as the softmax
+      // has stored that half of P; `wait_v`: the first of the two heads also waits for V_i.
       auto pv = [&](int w, int i, bool wait_v) -> bool {
-        if (!mbar_wait_warp(bar(PB_P + w), i & 1, abort_flag, F_MMA_P)) return false;
+        if (!mbar_wait_warp(bar(PB_P + 2 * w), i & 1, abort_flag, F_MMA_P)) return false;
         const int itv = 2 * i + 1, bv = itv % PNB;
         if (wait_v && !mbar_wait_warp(bar(PB_FULL + bv), (itv / PNB) & 1, abort_flag, F_MMA_V)) return false;
         tc_fence_after();
         const uint32_t vb = sbase + P_SM_KV + (uint32_t)bv * TILE;
-        gemm_ts8(tmem + 256u + (uint32_t)w * 128u, tmem + (uint32_t)w * 128u, desc_mn(vb), ID_PV, i > 0 ? 1u : 0u);
+        const uint32_t od = tmem + 256u + (uint32_t)w * 128u, pa = tmem + (uint32_t)w * 128u;
+        gemm_ts4(od, pa, desc_mn(vb), ID_PV, i > 0 ? 1u : 0u);
+        if (!mbar_wait_warp(bar(PB_P + 2 * w + 1), i & 1, abort_flag, F_MMA_P)) return false;
+        tc_fence_after();
+        gemm_ts4(od, pa + 32u, desc_mn(vb + 4u * 2048u), ID_PV, 1u);
         mma_commit_one(bar(PB_O + w));
         return true;
       };
@@ -1012,112 +1038,86 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
         ps_s[row] = (int32_t)routed_pos(p, h, tl.group, tl.slot0 + row);
         named_sync(1 + w, 128);
       }
-      if (!mbar_wait(bar(PB_S + w), j & 1, abort_flag, F_SOFTMAX_S)) {
+      if (!mbar_wait_warp(bar(PB_S + w), j & 1, abort_flag, F_SOFTMAX_S)) {
         ok = false;
         break;
       }
       // P_w(j-1) V_{j-1} was issued before S_w(j), so it has completed by now (in-order tensor
       // pipe): this wait returns at once and keeps the O barrier's phases in step.
-      if (j > 0 && !mbar_wait(bar(PB_O + w), (j - 1) & 1, abort_flag, F_SOFTMAX_O)) {
+      if (j > 0 && !mbar_wait_warp(bar(PB_O + w), (j - 1) & 1, abort_flag, F_SOFTMAX_O)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      bool done = !own;
-      const MaskLimits ml = (own && tl.masked) ? mask_limits(tl.kind, tl.k0, tl.group, p, qpos, qgroup)
-                                               : MaskLimits{127, 128, 0};
-      if (own && m_ref > -1.0e20f) {
-        // Single pass against the current reference max: P = exp2(s * c - m_ref) is formed for
-        // all 128 columns (held packed in registers) while the tile max is found. It is stored
-        // when the tile max does not pass the reference by more than 2^RESCALE_LOG2, which is
-        // exactly the case in which the two-pass path below keeps m_ref, so both paths produce
-        // the same bits (same products, same summation order). S is untouched until then.
-        uint32_t pk[64];
-        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        float ls[4] = {0.f, 0.f, 0.f, 0.f};
-        const float neg = -m_ref;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float s[32];
-          tmem_ld32(scol + 32u * q, s);
-          if (tl.masked) mask_cols<32>(s, 32 * q, tl.kind, ml, ps_s);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            mx4[i & 3] = fmaxf(mx4[i & 3], fmaxf(s[2 * i], s[2 * i + 1]));
-            const float a = fast_exp2(fmaf(s[2 * i], c, neg));
-            const float b = fast_exp2(fmaf(s[2 * i + 1], c, neg));
-            ls[i & 3] += a + b;
-            pk[16 * q + i] = pack2<T>(a, b);
-          }
-        }
-        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-        if (!(mx * c > m_ref + RESCALE_LOG2)) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) tmem_st16(scol + 16u * q, pk + 16 * q);
-          l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-          done = true;
-        }
-      }
-      if (!done) {
-        // Pass 1: row max over the two 64-column halves of S (re-read in pass 2, so only 64
-        // scores are live at a time).
+      bool lo_done = false;
+      if (own) {
+        // The whole S row in registers (one TMEM load), its exact max, then P = exp2(s * c - m_ref)
+        // written as packed 16-bit pairs over S columns [0, 64) in four 16-column stores.
+        const MaskLimits ml = tl.masked ? mask_limits(tl.kind, tl.k0, tl.group, p, qpos, qgroup)
+                                        : MaskLimits{127, 128, 0};
+        float s[128];
+        tmem_ld128(scol, s);
+        if (tl.masked) mask_cols<128>(s, 0, tl.kind, ml, ps_s);
         float mx8[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
-#pragma unroll 1
-        for (int half = 0; half < 2; ++half) {
-          float s[64];
-          tmem_ld64(scol + 64u * half, s);
-          if (tl.masked) mask_half(s, half, tl.kind, ml, ps_s);
+        for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(s[k], s[8 + k]);
 #pragma unroll
-          for (int i = 0; i < 64; i += 8)
+        for (int i = 16; i < 128; i += 16)
 #pragma unroll
-            for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], s[i + k]);
-        }
-        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+          for (int k = 0; k < 8; ++k) mx8[k] = fmax3(mx8[k], s[i + k], s[i + 8 + k]);
+        const float mx = fmaxf(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], fmax3(mx8[5], mx8[6], mx8[7])));
         const float mt = mx * c;
+        // Lazy rescale: the reference max moves only when the tile max passes it by more than
+        // 2^RESCALE_LOG2, so P stays below 2^RESCALE_LOG2 and most tiles leave O untouched.
+        float alpha = 1.f;
+        bool rescale_o = false;
         if (mt > m_ref + RESCALE_LOG2) {
-          const float alpha = fast_exp2(m_ref - mt);
-          if (j > 0 && m_ref > -1.0e20f) {
-#pragma unroll 1
-            for (int q4 = 0; q4 < 4; ++q4) {
-              float o[32];
-              tmem_ld32(ocol + q4 * 32, o);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] *= alpha;
-              tmem_st32(ocol + q4 * 32, o);
-            }
-          }
+          alpha = fast_exp2(m_ref - mt);
+          rescale_o = j > 0 && m_ref > -1.0e20f;
           l *= alpha;
           m_ref = mt;
         }
-        // Pass 2: P = exp2(s * c - m_ref), written as packed 16-bit pairs over S columns
-        // [0, 64); half h of S (columns 64h..64h+63) becomes P columns 32h..32h+31, so the
-        // second half is read before anything overwrites it.
+        // The O rescale uses warp-wide TMEM loads/stores, so it is decided per warp: lanes that
+        // keep their reference multiply by exactly 1. A warp that rescales holds back its
+        // first-half arrive until O is rescaled (the first P.V half accumulates into O).
+        if (!rescale_o) alpha = 1.f;
+        const bool warp_rescale = __any_sync(0xffffffffu, rescale_o);
         float ls[4] = {0.f, 0.f, 0.f, 0.f};
         const float neg = -m_ref;
-#pragma unroll 1
-        for (int half = 0; half < 2; ++half) {
-          float s[64];
-          tmem_ld64(scol + 64u * half, s);
-          if (tl.masked) mask_half(s, half, tl.kind, ml, ps_s);
+        const uint64_t c2 = f2_pack(c, c), n2 = f2_pack(neg, neg);
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            uint32_t pk[16];
+        for (int q = 0; q < 4; ++q) {
+          uint32_t pk[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float a = fast_exp2(fmaf(s[32 * q + 2 * i], c, neg));
-              const float b = fast_exp2(fmaf(s[32 * q + 2 * i + 1], c, neg));
-              ls[i & 3] += a + b;
-              pk[i] = pack2<T>(a, b);
-            }
-            tmem_st16(scol + 32u * half + 16u * q, pk);
+          for (int i = 0; i < 16; ++i) {
+            float xa, xb;
+            f2_unpack(f2_fma(f2_pack(s[32 * q + 2 * i], s[32 * q + 2 * i + 1]), c2, n2), xa, xb);
+            const float a = fast_exp2(xa), b = fast_exp2(xb);
+            ls[i & 3] += a + b;
+            pk[i] = pack2<T>(a, b);
+          }
+          tmem_st16(scol + 16u * q, pk);
+          if (q == 1 && !warp_rescale) {
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar(PB_P + 2 * w));
           }
         }
+        lo_done = !warp_rescale;
         l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      }
-      if (!own) {
+        // O(j-1) is complete (waited above) and no part of P(j).V(j) is issued before this warp's
+        // first-half arrive below.
+        if (warp_rescale) {
+#pragma unroll 1
+          for (int q4 = 0; q4 < 4; ++q4) {
+            float o[32];
+            tmem_ld32(ocol + q4 * 32, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(ocol + q4 * 32, o);
+          }
+        }
+      } else {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) pk[i] = 0u;
@@ -1126,11 +1126,12 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(PB_P + w));
+      if (!lo_done) mbar_arrive(bar(PB_P + 2 * w));
+      mbar_arrive(bar(PB_P + 2 * w + 1));
       if (own && tl.kind == 1) named_sync(1 + w, 128);
     }
     bool have_o = false;
-    if (ok && nt > 0) have_o = mbar_wait(bar(PB_O + w), (nt - 1) & 1, abort_flag, F_EPI_O);
+    if (ok && nt > 0) have_o = mbar_wait_warp(bar(PB_O + w), (nt - 1) & 1, abort_flag, F_EPI_O);
     tc_fence_after();
     const int64_t lrow = row0 + row;
     const bool store = lrow < row1;
