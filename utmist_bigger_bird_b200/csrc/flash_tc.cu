@@ -6,11 +6,13 @@
 // [q-W+1, q] and the routed keys idx[h, group(q), :] in [front, q-W]; scores q.k*scale*log2(e),
 // exp2, P rounded to the input dtype before P.V, output acc / max(l, 1e-20), fully masked rows 0.
 //
-// One CTA computes a 128-query tile of one query head (grid.z splits the tile's key range for the
-// exact tail). 192 threads:
+// flash_tc_kernel: one CTA computes a 128-query tile of one query head (grid.z splits the tile's
+// key range for the exact tail); used for odd GQA groups. flash_tc_pair_kernel (further below)
+// computes two query heads of one KV head per CTA and is used otherwise. flash_tc_kernel, 192
+// threads:
 //   warp 0      producer: Q, and every contiguous (sink/window) K/V tile by TMA (128B swizzle);
 //               routed K/V rows gathered with cp.async into the same swizzled layout.
-//   warp 1      allocates TMEM and issues the MMAs from one thread:
+//   warp 1      allocates TMEM and issues the MMAs (one elected lane):
 //                 S_j = Q K_j^T   (SS: A = Q smem K-major, B = K smem K-major) into S[j % 2]
 //                 O  += P_j V_j   (TS: A = P in TMEM over S[j % 2], B = V smem MN-major) into O
 //               S_{j+1} is issued before O += P_j V_j so the tensor core overlaps the softmax.
