@@ -155,7 +155,13 @@ uint64_t bb_kernel_launches(void) { return bb::g_launches.load(std::memory_order
 
 int bb_device_fault(int* code) {
   if (!code) return bb::fail(BB_ERR_ARG, "device_fault: null pointer");
-  return bb::device_fault_take(code);
+  int a = 0, b = 0;
+  int st = bb::flash_fault_take(&a);
+  if (st != BB_OK) return st;
+  st = bb::routes_fault_take(&b);
+  if (st != BB_OK) return st;
+  *code = a ? a : b;
+  return BB_OK;
 }
 
 int bb_rope_inplace(void* x, int dtype, int64_t B, int64_t H, int64_t T, int64_t D, int64_t sxb,

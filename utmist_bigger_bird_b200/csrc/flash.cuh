@@ -29,7 +29,9 @@ struct FlashParams {
 
 int flash_tc_launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream);
 int flash_tc_splits(const bb_flash_args* a, int sms);
-// Reads and clears the current device's fault word (set by a kernel whose bounded wait gave up).
-int device_fault_take(int* code);
+// Read and clear the current device's fault words (set by a kernel whose bounded wait gave up):
+// one for the attention kernels, one for the tcgen05 routing kernels.
+int flash_fault_take(int* code);
+int routes_fault_take(int* code);
 
 }  // namespace bb

@@ -9,6 +9,9 @@
 //   3. route_topk: per query head, an 8-bit radix select of the budget-th largest column score,
 //      then an index-ordered compaction, so the routes come out sorted ascending (:173).
 //
+// For head_dim 128 the two score passes run on tcgen05 instead (routes_tc.cu); merge and top-k
+// are shared. The mma.sync passes below serve the other head sizes and row paddings.
+//
 // Rows of a CTA are laid out head-major with each head's r routing queries padded to a multiple
 // of 16, so every 16-row MMA tile belongs to exactly one query head and pooling is a fixed-order
 // reduction (deterministic run to run).
@@ -16,6 +19,7 @@
 #include <mutex>
 
 #include "bb_common.cuh"
+#include "routes_tc.cuh"
 
 namespace bb {
 namespace {
@@ -434,6 +438,7 @@ int64_t slice_start(int64_t n, int64_t s) {  // Python slice start semantics for
 
 struct RtPlan {
   int64_t r_pad, heads_per_block, row_blocks, chunks, groups;
+  bool tc;                                        // tcgen05 score passes (routes_tc.cu)
   size_t partial_bytes, stats_bytes, col_bytes;   // stats_bytes = partials + merged rows
 };
 
@@ -448,9 +453,17 @@ int plan_routes(const bb_routes_args* a, RtPlan* pl) {
   if (a->budget < 0 || a->budget > a->n) return fail(BB_ERR_ARG, "routes: bad budget");
   pl->groups = a->heads / a->kv_heads;
   pl->r_pad = (a->r + 15) / 16 * 16;
-  pl->heads_per_block = std::max<int64_t>(1, std::min<int64_t>(pl->groups, RT_ROWS / pl->r_pad));
-  pl->row_blocks = cdiv(pl->groups, pl->heads_per_block);
-  pl->chunks = cdiv(a->n, RT_CHUNK);
+  pl->tc = routes_tc_eligible(a->d, pl->r_pad, pl->groups, a->dtype);
+  if (pl->tc) {
+    // One row block of RT_ROWS rows per KV head; a statistics "chunk" per CTA of the KV head.
+    pl->heads_per_block = pl->groups;
+    pl->row_blocks = 1;
+    pl->chunks = routes_tc_cpk(a->kv_heads, a->n);
+  } else {
+    pl->heads_per_block = std::max<int64_t>(1, std::min<int64_t>(pl->groups, RT_ROWS / pl->r_pad));
+    pl->row_blocks = cdiv(pl->groups, pl->heads_per_block);
+    pl->chunks = cdiv(a->n, RT_CHUNK);
+  }
   pl->partial_bytes = align_up((size_t)a->kv_heads * pl->row_blocks * RT_ROWS * pl->chunks * sizeof(float2), 256);
   pl->stats_bytes = pl->partial_bytes + align_up((size_t)a->kv_heads * pl->row_blocks * RT_ROWS * sizeof(float2), 256);
   pl->col_bytes = a->out_col ? 0 : align_up((size_t)a->heads * a->n * sizeof(float), 256);
@@ -473,17 +486,35 @@ int launch_routes_t(const bb_routes_args* a, const RtPlan& pl, char* ws, cudaStr
   p.stats = reinterpret_cast<float2*>(ws);
   p.merged = reinterpret_cast<float2*>(ws + pl.partial_bytes);
   p.col = a->out_col ? a->out_col : reinterpret_cast<float*>(ws + pl.stats_bytes);
-  const size_t smem = RtSmem<DP>::bytes;
-  cudaFuncSetAttribute(route_stats_kernel<T, DP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  cudaFuncSetAttribute(route_col_kernel<T, DP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  dim3 grid((unsigned)pl.chunks, (unsigned)a->kv_heads, (unsigned)pl.row_blocks);
-  route_stats_kernel<T, DP><<<grid, RT_THREADS, smem, stream>>>(p);
-  BB_CHECK_LAUNCH("route_stats_kernel");
   const int64_t rows = a->kv_heads * pl.row_blocks * RT_ROWS;
-  route_merge_kernel<<<(unsigned)cdiv(rows, 8), 256, 0, stream>>>(p.stats, p.merged, rows, pl.chunks);
-  BB_CHECK_LAUNCH("route_merge_kernel");
-  route_col_kernel<T, DP><<<grid, RT_THREADS, smem, stream>>>(p);
-  BB_CHECK_LAUNCH("route_col_kernel");
+  if (pl.tc) {
+    RtTcArgs t;
+    t.q = a->q; t.sq_h = a->sq_h; t.sq_t = a->sq_t;
+    t.k = a->k; t.sk_h = a->sk_h; t.sk_t = a->sk_t;
+    t.qpos = a->qpos;
+    t.n = a->n; t.r = a->r; t.r_pad = pl.r_pad; t.groups = pl.groups; t.kv_heads = a->kv_heads;
+    t.cpk = pl.chunks;
+    t.scaling = a->scaling; t.pool = a->pool; t.dtype = a->dtype;
+    t.lo_end = p.lo_end; t.hi_start = p.hi_start;
+    t.stats = p.stats; t.merged = p.merged; t.col = p.col;
+    int st = routes_tc_stats(t, stream);
+    if (st) return st;
+    route_merge_kernel<<<(unsigned)cdiv(rows, 8), 256, 0, stream>>>(p.stats, p.merged, rows, pl.chunks);
+    BB_CHECK_LAUNCH("route_merge_kernel");
+    st = routes_tc_col(t, stream);
+    if (st) return st;
+  } else {
+    const size_t smem = RtSmem<DP>::bytes;
+    cudaFuncSetAttribute(route_stats_kernel<T, DP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(route_col_kernel<T, DP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dim3 grid((unsigned)pl.chunks, (unsigned)a->kv_heads, (unsigned)pl.row_blocks);
+    route_stats_kernel<T, DP><<<grid, RT_THREADS, smem, stream>>>(p);
+    BB_CHECK_LAUNCH("route_stats_kernel");
+    route_merge_kernel<<<(unsigned)cdiv(rows, 8), 256, 0, stream>>>(p.stats, p.merged, rows, pl.chunks);
+    BB_CHECK_LAUNCH("route_merge_kernel");
+    route_col_kernel<T, DP><<<grid, RT_THREADS, smem, stream>>>(p);
+    BB_CHECK_LAUNCH("route_col_kernel");
+  }
   if (a->budget > 0) {
     route_topk_kernel<<<(unsigned)a->heads, TK_THREADS, 0, stream>>>(p.col, a->n, a->budget,
                                                                     a->out_idx, a->so_h);
