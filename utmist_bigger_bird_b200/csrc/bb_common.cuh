@@ -52,6 +52,20 @@ template <> struct Elem<float> {
   static __device__ __forceinline__ float round(float x) { return x; }
 };
 
+// Two values rounded to the 16-bit input type at once (one packed conversion, then the halves
+// are widened back with a shift and a mask): a <- round(a), b <- round(b).
+template <typename T> __device__ __forceinline__ void round2(float& a, float& b);
+template <> __device__ __forceinline__ void round2<__nv_bfloat16>(float& a, float& b) {
+  uint32_t p;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(a), "f"(b));  // high half = a, low half = b
+  a = __uint_as_float(p & 0xFFFF0000u);
+  b = __uint_as_float(p << 16);
+}
+template <> __device__ __forceinline__ void round2<__half>(float& a, float& b) {
+  a = Elem<__half>::round(a);
+  b = Elem<__half>::round(b);
+}
+
 // Pack two floats into a bf16x2 / f16x2 register (low half = a).
 template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b);
 template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
@@ -118,7 +132,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 
 // Packed fp32 pairs (sm_100): one instruction does two independent round-to-nearest operations,
-// so the softmax issues half as many FMA instructions with bit-identical results.
+// so the softmax loops issue half as many FMA/ADD instructions with bit-identical results.
 __device__ __forceinline__ uint64_t f2_pack(float a, float b) {
   uint64_t r;
   asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
@@ -130,6 +144,11 @@ __device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
 __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t r;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
 // Three-input maximum (sm_100).

@@ -340,6 +340,7 @@ __global__ void __launch_bounds__(RT_THREADS, 2) route_col_kernel(RtParams p) {
 
 // ----------------------------------------------------------------------------- top-k
 constexpr int TK_THREADS = 1024;
+constexpr int TK_VEC = 16;  // scores per thread per chunk
 
 __device__ __forceinline__ uint32_t order_key(float f) {
   const uint32_t u = __float_as_uint(f);
@@ -372,6 +373,44 @@ __device__ __forceinline__ int block_scan(int v, int* warp_sums, int& total) {
   return res;
 }
 
+// Scores of elements [i0, i0 + 16) as order keys; bit e of the result marks element i0 + e < n.
+__device__ __forceinline__ unsigned load16_keys(const float* __restrict__ c, int64_t i0, int64_t n, bool vec,
+                                                uint32_t (&u)[TK_VEC]) {
+  if (vec && i0 + TK_VEC <= n) {
+    const float4* p4 = reinterpret_cast<const float4*>(c + i0);
+#pragma unroll
+    for (int v = 0; v < TK_VEC / 4; ++v) {
+      const float4 f = __ldg(p4 + v);
+      u[4 * v] = order_key(f.x);
+      u[4 * v + 1] = order_key(f.y);
+      u[4 * v + 2] = order_key(f.z);
+      u[4 * v + 3] = order_key(f.w);
+    }
+    return 0xFFFFu;
+  }
+  unsigned valid = 0;
+#pragma unroll
+  for (int e = 0; e < TK_VEC; ++e) {
+    const bool ok = i0 + e < n;
+    u[e] = ok ? order_key(__ldg(c + i0 + e)) : 0u;
+    valid |= (ok ? 1u : 0u) << e;
+  }
+  return valid;
+}
+
+// The lowest k set bits of m.
+__device__ __forceinline__ unsigned lowest_bits(unsigned m, int k) {
+  unsigned r = 0;
+  for (int i = 0; i < k && m; ++i) {
+    const unsigned b = m & (0u - m);
+    r |= b;
+    m ^= b;
+  }
+  return r;
+}
+
+// One CTA per query head. Each thread owns 16 consecutive scores of a 16K-score chunk (vector
+// loads, 16x fewer dependent iterations than one score per thread).
 __global__ void __launch_bounds__(TK_THREADS) route_topk_kernel(const float* __restrict__ col,
                                                                 int64_t n, int64_t budget,
                                                                 int32_t* __restrict__ out,
@@ -384,16 +423,38 @@ __global__ void __launch_bounds__(TK_THREADS) route_topk_kernel(const float* __r
   const float* c = col + h * n;
   int32_t* o = out + h * so_h;
   if (budget <= 0) return;
+  const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(c) & 15) == 0);
+  constexpr int64_t CHUNK = (int64_t)TK_THREADS * TK_VEC;
   uint32_t prefix = 0, pmask = 0;
   int64_t rem = budget;
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
     for (int i = threadIdx.x; i < 256; i += TK_THREADS) hist[i] = 0;
     __syncthreads();
-    for (int64_t i = threadIdx.x; i < n; i += TK_THREADS) {
-      const uint32_t u = order_key(c[i]);
-      if ((u & pmask) == prefix) atomicAdd(&hist[(u >> shift) & 255u], 1u);
+    // Column scores are close in magnitude, so one digit is often shared by most keys (the top
+    // byte always is): each thread counts hits on the bin of its first key in a register and adds
+    // them once, instead of one shared-memory atomic per key on the same word.
+    uint32_t hot = 0xFFFFFFFFu;
+    unsigned int hot_cnt = 0;
+    for (int64_t base = 0; base < n; base += CHUNK) {
+      uint32_t u[TK_VEC];
+      const unsigned valid = load16_keys(c, base + (int64_t)threadIdx.x * TK_VEC, n, vec, u);
+#pragma unroll
+      for (int e = 0; e < TK_VEC; ++e) {
+        if (((valid >> e) & 1u) && (u[e] & pmask) == prefix) {
+          const uint32_t bin = (u[e] >> shift) & 255u;
+          if (bin == hot) {
+            ++hot_cnt;
+          } else if (hot_cnt == 0) {
+            hot = bin;
+            hot_cnt = 1;
+          } else {
+            atomicAdd(&hist[bin], 1u);
+          }
+        }
+      }
     }
+    if (hot_cnt) atomicAdd(&hist[hot], hot_cnt);
     __syncthreads();
     if (threadIdx.x == 0) {
       int64_t cum = 0;
@@ -414,20 +475,37 @@ __global__ void __launch_bounds__(TK_THREADS) route_topk_kernel(const float* __r
   // prefix = key of the budget-th largest score; take every key above it and the first `rem`
   // keys equal to it, in index order.
   int64_t written = 0, eq_seen = 0;
-  for (int64_t base = 0; base < n; base += TK_THREADS) {
-    const int64_t i = base + threadIdx.x;
-    const uint32_t u = i < n ? order_key(c[i]) : 0u;
-    const int gt = (i < n && u > prefix) ? 1 : 0;
-    const int eq = (i < n && u == prefix) ? 1 : 0;
+  for (int64_t base = 0; base < n && written < budget; base += CHUNK) {
+    const int64_t i0 = base + (int64_t)threadIdx.x * TK_VEC;
+    uint32_t u[TK_VEC];
+    const unsigned valid = load16_keys(c, i0, n, vec, u);
+    unsigned gtm = 0, eqm = 0;
+#pragma unroll
+    for (int e = 0; e < TK_VEC; ++e) {
+      if ((valid >> e) & 1u) {
+        gtm |= (u[e] > prefix ? 1u : 0u) << e;
+        eqm |= (u[e] == prefix ? 1u : 0u) << e;
+      }
+    }
+    const int eq_cnt = __popc(eqm);
     int eq_total;
-    const int eq_incl = block_scan(eq, warp_sums, eq_total);
-    const int take = gt || (eq && (eq_seen + eq_incl - 1) < rem);
+    const int eq_incl = block_scan(eq_cnt, warp_sums, eq_total);
+    const int64_t eq_before = eq_seen + eq_incl - eq_cnt;
+    const int64_t eq_take = rem - eq_before < 0 ? 0 : (rem - eq_before > eq_cnt ? eq_cnt : rem - eq_before);
+    const unsigned takem = gtm | lowest_bits(eqm, (int)eq_take);
+    const int tk = __popc(takem);
     int take_total;
-    const int take_incl = block_scan(take, warp_sums, take_total);
-    if (take && written + take_incl - 1 < budget) o[written + take_incl - 1] = (int32_t)i;
+    const int take_incl = block_scan(tk, warp_sums, take_total);
+    int64_t pos = written + take_incl - tk;
+#pragma unroll
+    for (int e = 0; e < TK_VEC; ++e) {
+      if ((takem >> e) & 1u) {
+        if (pos < budget) o[pos] = (int32_t)(i0 + e);
+        ++pos;
+      }
+    }
     written += take_total;
     eq_seen += eq_total;
-    if (written >= budget) break;
   }
 }
 
@@ -453,7 +531,7 @@ int plan_routes(const bb_routes_args* a, RtPlan* pl) {
   if (a->budget < 0 || a->budget > a->n) return fail(BB_ERR_ARG, "routes: bad budget");
   pl->groups = a->heads / a->kv_heads;
   pl->r_pad = (a->r + 15) / 16 * 16;
-  pl->tc = routes_tc_eligible(a->d, pl->r_pad, pl->groups, a->dtype);
+  pl->tc = routes_tc_eligible(a->d, pl->r_pad, pl->groups, a->dtype, a->scaling);
   if (pl->tc) {
     // One row block of RT_ROWS rows per KV head; a statistics "chunk" per CTA of the KV head.
     pl->heads_per_block = pl->groups;

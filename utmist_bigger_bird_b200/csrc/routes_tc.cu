@@ -67,11 +67,11 @@ __device__ __forceinline__ int64_t row_position(const RtTcArgs& a, int i) {
 // cp.async (zero rows for padding). SPLIT: two 128-row halves, each [2 d-halves][128][64] (pass
 // 1, A operand); otherwise [2 d-halves][256][64] (pass 2, B operand with N = 256).
 template <typename T, bool SPLIT>
-__device__ __forceinline__ void load_rows(const RtTcArgs& a, uint32_t qs, int64_t kv, int lane) {
+__device__ __forceinline__ void load_rows(const RtTcArgs& a, uint32_t qs, int64_t kv, int lane, const int64_t* rowpos) {
   const T* q = static_cast<const T*>(a.q);
   for (int idx = lane; idx < ROWS * 16; idx += 32) {
     const int i = idx >> 4, c = idx & 15;
-    const int64_t ps = row_position(a, i);
+    const int64_t ps = rowpos[i];
     const T* src = q;
     if (ps >= 0) src = q + (kv * a.groups + i / (int)a.r_pad) * a.sq_h + ps * a.sq_t + c * 8;
     uint32_t dst;
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(THREADS, 1) rt_stats_kernel(const __grid_const
 
   if (warp == 0) {
     if (nt > 0) {
-      load_rows<T, true>(a, sbase + SM_Q, kv, lane);
+      load_rows<T, true>(a, sbase + SM_Q, kv, lane, rowpos);
       mbar_arrive_one(bar(B_Q));
       produce_k(&kmap, kswap, kv, t0, nt, sbase, abort_flag, bars);
     }
@@ -204,16 +204,14 @@ __global__ void __launch_bounds__(THREADS, 1) rt_stats_kernel(const __grid_const
       mbar_arrive(bar(B_SE + sb));
       if (qp < 0) continue;
       const int64_t key0 = (t0 + it) * 128;
-      if (key0 + 127 <= qp && key0 + 128 <= a.n) {
+      // Dtype-rounded dot products; the (positive) scale is applied inside the exponent below,
+      // so the row max is taken on the unscaled values.
 #pragma unroll
-        for (int i = 0; i < 128; ++i) s[i] = Elem<T>::round(s[i]) * c2;
-      } else {
+      for (int i = 0; i < 128; i += 2) round2<T>(s[i], s[i + 1]);
+      if (!(key0 + 127 <= qp && key0 + 128 <= a.n)) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          const int64_t key = key0 + i;
-          const float v = Elem<T>::round(s[i]) * c2;
-          s[i] = (key > qp || key >= a.n) ? -INFINITY : v;
-        }
+        for (int i = 0; i < 128; ++i)
+          if (key0 + i > qp || key0 + i >= a.n) s[i] = -INFINITY;
       }
       float mx8[8];
 #pragma unroll
@@ -222,15 +220,27 @@ __global__ void __launch_bounds__(THREADS, 1) rt_stats_kernel(const __grid_const
       for (int i = 16; i < 128; i += 16)
 #pragma unroll
         for (int k = 0; k < 8; ++k) mx8[k] = fmax3(mx8[k], s[i + k], s[i + 8 + k]);
-      const float mt = fmaxf(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], fmax3(mx8[5], mx8[6], mx8[7])));
+      const float mt =
+          c2 * fmaxf(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], fmax3(mx8[5], mx8[6], mx8[7])));
       if (mt > m + RESCALE) {
         if (m > -INFINITY) l *= fast_exp2(m - mt);
         m = mt;
       }
       if (m == -INFINITY) continue;
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      // l += sum_i exp2(s_i * c2 - m), two lanes of the sum per packed add.
+      const uint64_t c22 = f2_pack(c2, c2), nm2 = f2_pack(-m, -m);
+      uint64_t l01 = f2_pack(0.f, 0.f), l23 = f2_pack(0.f, 0.f);
 #pragma unroll
-      for (int i = 0; i < 128; ++i) ls[i & 3] += fast_exp2(s[i] - m);
+      for (int i = 0; i < 128; i += 4) {
+        float x0, x1, x2, x3;
+        f2_unpack(f2_fma(f2_pack(s[i], s[i + 1]), c22, nm2), x0, x1);
+        f2_unpack(f2_fma(f2_pack(s[i + 2], s[i + 3]), c22, nm2), x2, x3);
+        l01 = f2_add(l01, f2_pack(fast_exp2(x0), fast_exp2(x1)));
+        l23 = f2_add(l23, f2_pack(fast_exp2(x2), fast_exp2(x3)));
+      }
+      float ls[4];
+      f2_unpack(l01, ls[0], ls[1]);
+      f2_unpack(l23, ls[2], ls[3]);
       l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
     }
     // Natural-log statistics for the merge: sum_j exp(s_j - m * ln 2) = l.
@@ -292,7 +302,7 @@ __global__ void __launch_bounds__(THREADS, 1) rt_col_kernel(const __grid_constan
 
   if (warp == 0) {
     if (nt > 0) {
-      load_rows<T, false>(a, sbase + SM_Q, kv, lane);
+      load_rows<T, false>(a, sbase + SM_Q, kv, lane, rowpos);
       mbar_arrive_one(bar(B_Q));
       produce_k(&kmap, kswap, kv, t0, nt, sbase, abort_flag, bars);
     }
@@ -321,6 +331,7 @@ __global__ void __launch_bounds__(THREADS, 1) rt_col_kernel(const __grid_constan
     const uint32_t tl = tmem + ((uint32_t)(32 * wq) << 16) + 128u * (uint32_t)half;
     const float c2 = a.scaling * LOG2E_F;
     const float inv_r = 1.f / (float)a.r;
+    const bool max_pool = a.pool == BB_POOL_MAX;
     int64_t min_qp = (int64_t)1 << 62;
     for (int i = 0; i < ROWS; ++i)
       if (rowpos[i] >= 0 && rowpos[i] < min_qp) min_qp = rowpos[i];
@@ -336,21 +347,39 @@ __global__ void __launch_bounds__(THREADS, 1) rt_col_kernel(const __grid_constan
       const int64_t key0 = (t0 + it) * 128;
       const int64_t key = key0 + 32 * wq + lane;
       const bool causal_free = key0 + 127 <= min_qp;  // no routing row sees a key after its query
+      const uint64_t c22 = f2_pack(c2, c2);
 #pragma unroll
       for (int hh = 0; hh < HPH; ++hh) {
         const int rbase = 128 * half + hh * RP;
         if (rbase >= (int)(a.groups * a.r_pad)) break;
-        float acc = 0.f;
+        // p_j = exp2(round(s_j) * c2 + bias_j) for the head's RP rows, two rows per packed FMA.
+        uint64_t sum2 = f2_pack(0.f, 0.f);
+        float mx = 0.f;
 #pragma unroll
-        for (int j = 0; j < RP; ++j) {
-          const int row = rbase + j;
-          const float bias = rowbias[row];
-          float pr = fast_exp2(fmaf(Elem<T>::round(s[hh * RP + j]), c2, bias));
-          if (!causal_free && key > rowpos[row]) pr = 0.f;
-          acc = a.pool == BB_POOL_MAX ? fmaxf(acc, pr) : acc + pr;
+        for (int j = 0; j < RP; j += 2) {
+          float r0 = s[hh * RP + j], r1 = s[hh * RP + j + 1];
+          round2<T>(r0, r1);
+          const float2 bias = *reinterpret_cast<const float2*>(rowbias + rbase + j);
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(r0, r1), c22, f2_pack(bias.x, bias.y)), x0, x1);
+          float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+          if (!causal_free) {
+            if (key > rowpos[rbase + j]) p0 = 0.f;
+            if (key > rowpos[rbase + j + 1]) p1 = 0.f;
+          }
+          if (max_pool)
+            mx = fmax3(mx, p0, p1);
+          else
+            sum2 = f2_add(sum2, f2_pack(p0, p1));
+        }
+        float acc = mx;
+        if (!max_pool) {
+          float a0, a1;
+          f2_unpack(sum2, a0, a1);
+          acc = a0 + a1;
         }
         if (key < a.n) {
-          float v = a.pool == BB_POOL_MAX ? acc : acc * inv_r;
+          float v = max_pool ? acc : acc * inv_r;
           if (key < a.lo_end || key >= a.hi_start) v = -1.f;
           const int64_t head = kv * a.groups + rbase / (int)a.r_pad;
           a.col[head * a.n + key] = v;
@@ -408,8 +437,8 @@ int k_map(const RtTcArgs& a, CUtensorMap* m, int* swap) {
 
 }  // namespace rtc
 
-bool routes_tc_eligible(int64_t d, int64_t r_pad, int64_t groups, int dtype) {
-  return d == 128 && (dtype == BB_BF16 || dtype == BB_F16) && (r_pad == 16 || r_pad == 32 || r_pad == 64) &&
+bool routes_tc_eligible(int64_t d, int64_t r_pad, int64_t groups, int dtype, float scaling) {
+  return d == 128 && scaling > 0.f && (dtype == BB_BF16 || dtype == BB_F16) && (r_pad == 16 || r_pad == 32 || r_pad == 64) &&
          groups * r_pad <= rtc::ROWS && tc::encode_fn() != nullptr;
 }
 

@@ -24,8 +24,9 @@ struct RtTcArgs {
   float* col;                // [heads][n]
 };
 
-// True when the tcgen05 passes handle this shape.
-bool routes_tc_eligible(int64_t d, int64_t r_pad, int64_t groups, int dtype);
+// True when the tcgen05 passes handle this call (they take the row max on unscaled scores,
+// so the scale must be positive).
+bool routes_tc_eligible(int64_t d, int64_t r_pad, int64_t groups, int dtype, float scaling);
 // CTAs per KV head for this device.
 int64_t routes_tc_cpk(int64_t kv_heads, int64_t n);
 // Pass 1: per-row softmax statistics of each CTA's key range.
