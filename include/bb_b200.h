@@ -13,6 +13,8 @@
  *   bb_flash             kernels/bigger_bird_flash.py:99-138  bigger_bird_flash(q, k, v, indices, ...)
  *   bb_sparse_prefill    modal_rd/attention.py:176-206    RDAttention.sparse_prefill(q, k, v)
  *                        (+ the in-place RoPE of forward, modal_rd/attention.py:121, when cos/sin given)
+ *   bb_kv_evict          modal_rd/attention.py:226-259    RDAttention.evict(cache, q, k, v)
+ *                        (+ forward_pool, modal_rd/attention.py:70-75)
  */
 #ifndef BB_B200_H
 #define BB_B200_H
@@ -170,6 +172,37 @@ typedef struct {
 BB_API int bb_sparse_prefill_workspace_size(const bb_prefill_args* a, size_t* bytes);
 BB_API int bb_sparse_prefill(const bb_prefill_args* a, void* workspace, size_t workspace_bytes,
                       bb_stream_t stream);
+
+/*
+ * KV eviction after a sparse prefill (RDAttention.evict, modal_rd/attention.py:226-259): per KV
+ * head, keep the sink keys [0, sink), the `keep` best middle keys and the last `window` keys, and
+ * write the kept K/V rows (in position order) and their positions.
+ *   score[kv, j]  = max over the KV head's query heads of col[h, j]            (:243, :221)
+ *   pooled[kv, j] = max of score[kv, j - pool + 1 .. j + pool_back] (-inf off the ends; pool <= 1
+ *                   and pool_back == 0 leave score unchanged)                 (forward_pool :70-75)
+ *   prio[kv, j]   = 2 * (j is a route of any of its query heads) + pooled     (:247)
+ *   middle keys   = the `keep` largest prio among [sink, n - window), sorted ascending (:248-253;
+ *                   equal priorities at the cut are taken in position order)
+ * col: [H, n] fp32 column scores (the routing scores of the prefill, or exact-attention scores of
+ * the last queries for evict_obs); idx: [H, budget] int32 routes (entries outside [0, n) ignored);
+ * k, v: [Hk, n, d]; out_k, out_v: [Hk, sink + keep + window, d]; out_pos: [Hk, sink + keep +
+ * window] int64. Requires sink + window <= n and keep <= n - sink - window.
+ */
+typedef struct {
+  const float* col; int64_t sc_h;
+  const int32_t* idx; int64_t si_h; int64_t budget;
+  const void* k; int64_t sk_h, sk_t;
+  const void* v; int64_t sv_h, sv_t;
+  void* out_k; int64_t sok_h, sok_t;
+  void* out_v; int64_t sov_h, sov_t;
+  int64_t* out_pos;                      /* [Hk, sink + keep + window], contiguous */
+  int64_t heads, kv_heads, n, d;
+  int64_t sink, window, keep, pool, pool_back;
+  int dtype;                              /* BB_F16 / BB_BF16 / BB_F32 (element type of k, v) */
+} bb_evict_args;
+
+BB_API int bb_kv_evict_workspace_size(const bb_evict_args* a, size_t* bytes);
+BB_API int bb_kv_evict(const bb_evict_args* a, void* workspace, size_t workspace_bytes, bb_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -23,6 +23,10 @@ What it restates (paths inside the reference project derkychen/utmist-bigger-bir
                         query rows so long sequences stay tractable.
 * ``sparse_prefill`` -- ``modal_rd/attention.py:176-206`` (routes, optional ``vertical_scope``
                         groups, main pass, exact tail overwriting the last ``exact_tail`` rows).
+* ``forward_pool`` / ``evict_positions`` -- ``modal_rd/attention.py:70-75`` and ``:226-259``
+                        (``RDAttention.evict``): routed columns first, then the group-max (pooled)
+                        column scores, sink and kept window excluded, top-``keep`` sorted; the
+                        kept cache is the K/V rows at [sink | selected | window].
 
 Parity is pinned by ``tests/test_oracle_golden.py`` against vectors produced by the reference
 itself (``tests/golden/make_golden.py`` imports the reference read-only).
@@ -36,6 +40,7 @@ import numpy as np
 __all__ = [
     "bf16_round", "f16_round", "rounder", "rope", "vertical_budget", "route_query_positions",
     "route_scores", "routes", "topk_sorted", "route_sets_match", "flash", "sparse_prefill",
+    "forward_pool", "evict_positions",
 ]
 
 
@@ -295,3 +300,49 @@ def sparse_prefill(q, k, v, *, scaling, sink, window, vertical, vertical_sqrt=0.
                          kv_groups=g, scale=scaling, rows=rows[tail_rows] - (n - r), heads=heads)
             out[:, tail_rows] = tail
     return out, idx
+
+
+# ----------------------------------------------------------------------------- KV eviction
+def forward_pool(score, p, back=0):
+    """``modal_rd/attention.py:70-75``: [H, n] -> [H, n], each key takes the max of the scores of
+    keys j - p + 1 .. j + back (-inf beyond the ends; p is taken as at least 1)."""
+    score = np.asarray(score, dtype=np.float32)
+    p = max(int(p), 1)
+    H, n = score.shape
+    padded = np.full((H, n + p - 1 + back), -np.inf, dtype=np.float32)
+    padded[:, p - 1:p - 1 + n] = score
+    out = np.full((H, n), -np.inf, dtype=np.float32)
+    for o in range(p + back):
+        out = np.maximum(out, padded[:, o:o + n])
+    return out
+
+
+def evict_positions(idx, col, *, kv_heads, sink, window, evict_keep=0, evict_window=0, evict_pool=0,
+                    evict_pool_back=0):
+    """Kept positions ``[Hk, sink + keep + w]`` of ``RDAttention.evict`` (``modal_rd/attention.py:
+    226-259``) and the priorities they were selected by.
+
+    idx: [H, budget] routes; col: [H, n] fp32 per-query-head column scores (the routing scores, or
+    the ``evict_obs`` exact-attention scores before the group max). The middle keys are the top-
+    ``keep`` priorities sorted ascending; equal priorities at the cut go to the lower position."""
+    idx = np.asarray(idx)
+    col = np.asarray(col, dtype=np.float32)
+    H, n = col.shape
+    hk = kv_heads
+    g = H // hk
+    member = np.zeros((H, n), dtype=bool)
+    for h in range(H):
+        member[h, idx[h]] = True
+    score = col.reshape(hk, g, n).max(1)
+    if evict_pool > 1 or evict_pool_back:
+        score = forward_pool(score, evict_pool, evict_pool_back)
+    prio = member.reshape(hk, g, n).any(1).astype(np.float32) * np.float32(2) + score
+    w = min(max(window, evict_window), n - sink)
+    prio[:, :sink] = -np.inf
+    prio[:, n - w:] = -np.inf
+    budget = idx.shape[-1]
+    extra = min(max(evict_keep, g * budget) if evict_keep else g * budget, n - sink - w)
+    sel = topk_sorted(prio, extra).astype(np.int64)
+    ar = np.arange(n, dtype=np.int64)
+    pos = np.concatenate([np.tile(ar[:sink], (hk, 1)), sel, np.tile(ar[n - w:], (hk, 1))], axis=1)
+    return pos, prio

@@ -114,6 +114,22 @@ EXTRA_ROUTE_CONFIGS = {
 }
 
 
+# KV eviction after the prefill (RDAttention.evict, modal_rd/attention.py:226-259): the default
+# policy and each tuning knob of the reference's eviction tests, on the PREFILL_SHAPE inputs.
+EVICT_BASE_KW = dict(sink=8, window=96, vertical=24, n_route=16)
+EVICT_CONFIGS = {
+    "default": {},
+    "keep160": dict(evict_keep=160),
+    "window160": dict(evict_window=160),
+    "pool8": dict(evict_pool=8),
+    "back8": dict(evict_pool_back=8),
+    "obs24": dict(evict_obs=24),
+    "obs24max": dict(evict_obs=24, evict_obs_max=True),
+    "full1": dict(evict_full_layers=1),
+    "all": dict(evict_keep=160, evict_window=160, evict_pool=8, evict_obs=24, evict_pool_back=4),
+}
+
+
 def config1_rows(n):
     return torch.cat([torch.linspace(0, n - 300, 12).long(), torch.arange(n - 258, n - 254),
                       torch.arange(n - 4, n)])

@@ -133,6 +133,28 @@ def gen_config1():
     return out
 
 
+def gen_evict():
+    """KV eviction through the reference: routes of the prefill, then RDAttention.evict on a
+    one-layer cache. Stores the routes, the routing column scores and the kept positions."""
+    s = cases.PREFILL_SHAPE
+    out = {}
+    for dt, tag in ((torch.float32, "f32"), (torch.bfloat16, "bf16")):
+        q, k, v, _ = cases.prefill_inputs(dt)
+        for name, kw in cases.EVICT_CONFIGS.items():
+            attn = ref_attn.RDAttention(base(s["H"], s["hk"], s["d"]), kv_evict=True, **cases.EVICT_BASE_KW, **kw)
+            cache = SimpleNamespace(layers=[SimpleNamespace(keys=None, values=None)])
+            with torch.inference_mode():
+                attn.sparse_prefill(q, k, v)
+                idx, col = attn.last_routes.clone(), attn._col.clone()
+                attn.evict(cache, q, k, v)
+            rec = dict(idx=idx.numpy(), col=col.numpy(), kept=attn.kept.numpy())
+            if kw.get("evict_obs"):
+                with torch.inference_mode():
+                    rec["obs_scores"] = attn.evict_scores(q, k).numpy()
+            out[f"{tag}_{name}"] = rec
+    return out
+
+
 def save(name, groups):
     flat = {}
     for key, rec in groups.items():
@@ -148,3 +170,4 @@ if __name__ == "__main__":
     save("flash", gen_flash())
     save("prefill", gen_prefill())
     save("config1", gen_config1())
+    save("evict", gen_evict())

@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_struct_layouts_match_header(tmp_path):
     structs = {"bb_routes_args": _lib.RoutesArgs, "bb_flash_args": _lib.FlashArgs,
-               "bb_prefill_args": _lib.PrefillArgs}
+               "bb_prefill_args": _lib.PrefillArgs, "bb_evict_args": _lib.EvictArgs}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void) {"]
     for cname, py in structs.items():
         lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
@@ -134,3 +134,31 @@ def test_python_surface_rejects_cpu_tensors():
     attn = RDAttention(base)
     with pytest.raises(ValueError, match="CUDA"):
         attn.routes(q[None], q[None, :2])
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(sink=60, window=50), "sink + window <= n"),
+    (dict(keep=90), "keep must lie"),
+    (dict(heads=7), "multiple of kv_heads"),
+    (dict(dtype=9), "dtype"),
+    (dict(pool=-1), "pool"),
+])
+def test_kv_evict_host_validation(kw, msg):
+    """bb_kv_evict's argument checks run on the host (no device needed)."""
+    L = _lib.lib()
+    args = dict(heads=8, kv_heads=2, n=100, d=32, sink=8, window=16, keep=20, budget=4, dtype=_lib.BB_BF16)
+    args.update(kw)
+    a = _lib.EvictArgs(**args)
+    nbytes = C.c_size_t(0)
+    st = L.bb_kv_evict_workspace_size(C.byref(a), C.byref(nbytes))
+    assert st != 0 and msg in L.bb_last_error().decode()
+
+
+def test_kv_evict_workspace_size():
+    L = _lib.lib()
+    a = _lib.EvictArgs(heads=32, kv_heads=8, n=131072, d=128, sink=64, window=16384, keep=2048, budget=512,
+                       dtype=_lib.BB_BF16)
+    nbytes = C.c_size_t(0)
+    assert L.bb_kv_evict_workspace_size(C.byref(a), C.byref(nbytes)) == 0
+    cells = 8 * 131072
+    assert nbytes.value >= cells * (1 + 4 + 4) + 8 * 2048 * 4

@@ -122,3 +122,60 @@ def test_oracle_config1_matches_reference(golden, tag):
     ok, swapped, gap = orc.route_sets_match(idx, rec["idx"], col)
     assert ok, (swapped, gap)
     np.testing.assert_allclose(out, rec["out"], atol=5e-5 if tag == "f32" else 1e-2, rtol=1e-4)
+
+
+def kept_match(got, want, prio, sink, w, tol=0.0):
+    """Same shape; per KV head the kept sets agree except positions whose priority ties (within
+    ``tol``) with the lowest kept middle priority (torch.topk's order among ties is unspecified)."""
+    if got.shape != want.shape:
+        return False
+    for h in range(got.shape[0]):
+        diff = set(got[h].tolist()) ^ set(want[h].tolist())
+        if not diff:
+            continue
+        cut = prio[h, got[h][sink:got.shape[1] - w]].min()
+        if any(abs(float(prio[h, i]) - float(cut)) > tol for i in diff):
+            return False
+    return True
+
+
+@pytest.mark.parametrize("tag", ["f32", "bf16"])
+@pytest.mark.parametrize("name", list(cases.EVICT_CONFIGS))
+def test_oracle_evict_matches_reference(golden, tag, name):
+    """RDAttention.evict (modal_rd/attention.py:226-259) through the oracle: kept positions equal
+    the reference's up to ties at the cut; the evict_obs scores match evict_scores."""
+    g = golden("evict")[f"{tag}_{name}"]
+    kw, bkw, s = cases.EVICT_CONFIGS[name], cases.EVICT_BASE_KW, cases.PREFILL_SHAPE
+    n, hk, H, d = s["n"], s["hk"], s["H"], s["d"]
+    if kw.get("evict_full_layers"):
+        assert np.array_equal(g["kept"], np.tile(np.arange(n), (hk, 1)))
+        return
+    col, tol = g["col"], 0.0
+    if kw.get("evict_obs"):
+        dtype = torch.float32 if tag == "f32" else torch.bfloat16
+        q, k, _, _ = cases.prefill_inputs(dtype)
+        col = orc.route_scores(np32(q[0]), np32(k[0]), scaling=d ** -0.5, sink=0, window=0,
+                               n_route=kw["evict_obs"], pool="max" if kw.get("evict_obs_max") else "mean",
+                               queries="last", dtype=tag)
+        obs = col.reshape(hk, H // hk, n).max(1)
+        np.testing.assert_allclose(obs, g["obs_scores"], rtol=1e-5, atol=1e-8)
+        tol = 1e-6
+    pos, prio = orc.evict_positions(g["idx"], col, kv_heads=hk, sink=bkw["sink"], window=bkw["window"],
+                                    evict_keep=kw.get("evict_keep", 0), evict_window=kw.get("evict_window", 0),
+                                    evict_pool=kw.get("evict_pool", 0), evict_pool_back=kw.get("evict_pool_back", 0))
+    w = min(max(bkw["window"], kw.get("evict_window", 0)), n - bkw["sink"])
+    assert kept_match(pos, g["kept"], prio, bkw["sink"], w, tol)
+
+
+def test_oracle_forward_pool_spans():
+    """forward_pool (modal_rd/attention.py:70-75) on the span cases of tests/test_kv_evict.py:134-152."""
+    score = np.zeros((2, 20), dtype=np.float32)
+    score[0, 5], score[1, 18] = 1.0, 0.5
+    pooled = orc.forward_pool(score, 4)
+    assert (pooled[0, 5:9] == 1).all() and (pooled[0, :5] == 0).all() and (pooled[0, 9:] == 0).all()
+    assert (pooled[1, 18:] == 0.5).all() and (pooled[1, :18] == 0).all()
+    score = np.zeros((1, 20), dtype=np.float32)
+    score[0, 10] = 1.0
+    pooled = orc.forward_pool(score, 3, back=4)
+    assert (pooled[0, 6:13] == 1).all() and (pooled[0, :6] == 0).all() and (pooled[0, 13:] == 0).all()
+    assert (orc.forward_pool(score, 0, back=2)[0, 8:11] == 1).all()

@@ -61,6 +61,19 @@ class PrefillArgs(C.Structure):
                 ("scaling", f32), ("pool", C.c_int), ("dtype", C.c_int)]
 
 
+class EvictArgs(C.Structure):
+    _fields_ = [("col", vp), ("sc_h", i64),
+                ("idx", vp), ("si_h", i64), ("budget", i64),
+                ("k", vp), ("sk_h", i64), ("sk_t", i64),
+                ("v", vp), ("sv_h", i64), ("sv_t", i64),
+                ("out_k", vp), ("sok_h", i64), ("sok_t", i64),
+                ("out_v", vp), ("sov_h", i64), ("sov_t", i64),
+                ("out_pos", vp),
+                ("heads", i64), ("kv_heads", i64), ("n", i64), ("d", i64),
+                ("sink", i64), ("window", i64), ("keep", i64), ("pool", i64), ("pool_back", i64),
+                ("dtype", C.c_int)]
+
+
 EXPORTS = {
     "bb_last_error": (C.c_char_p, []),
     "bb_abi_version": (C.c_int, []),
@@ -74,6 +87,8 @@ EXPORTS = {
     "bb_flash": (C.c_int, [C.POINTER(FlashArgs), vp, C.c_size_t, vp]),
     "bb_sparse_prefill_workspace_size": (C.c_int, [C.POINTER(PrefillArgs), C.POINTER(C.c_size_t)]),
     "bb_sparse_prefill": (C.c_int, [C.POINTER(PrefillArgs), vp, C.c_size_t, vp]),
+    "bb_kv_evict_workspace_size": (C.c_int, [C.POINTER(EvictArgs), C.POINTER(C.c_size_t)]),
+    "bb_kv_evict": (C.c_int, [C.POINTER(EvictArgs), vp, C.c_size_t, vp]),
 }
 
 _lib = None

@@ -138,3 +138,42 @@ def sparse_prefill_(q, k, v, qpos, out, out_idx, *, sink, window, budget, exact_
     ws = _workspace(nbytes.value, q.device)
     _lib.check(L.bb_sparse_prefill(C.byref(a), _ptr(ws), nbytes.value, _stream(q)), "sparse_prefill")
     return out
+
+
+def kv_evict_(idx: torch.Tensor | None, col: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+              sink: int, window: int, keep: int, pool: int = 0, pool_back: int = 0):
+    """KV eviction (RDAttention.evict, reference modal_rd/attention.py:226-259) in one C call.
+
+    idx [H, budget] int32 routes (or None), col [H, n] fp32 column scores, k/v [Hk, n, d] ->
+    (k_kept [Hk, L, d], v_kept [Hk, L, d], pos [Hk, L] int64) with L = sink + keep + window."""
+    if not (k.is_cuda and v.is_cuda and col.is_cuda):
+        raise ValueError("kv_evict requires CUDA tensors")
+    if k.dtype not in _DT or v.dtype != k.dtype or col.dtype != torch.float32:
+        raise ValueError("kv_evict: k and v must share one of f16/bf16/f32; col must be float32")
+    k, v = rows_view(k), rows_view(v)
+    col = col if col.stride(-1) == 1 else col.contiguous()
+    Hk, n, d = k.shape
+    H = col.shape[0]
+    L = sink + keep + window
+    out_k = torch.empty((Hk, L, d), dtype=k.dtype, device=k.device)
+    out_v = torch.empty((Hk, L, d), dtype=v.dtype, device=v.device)
+    pos = torch.empty((Hk, L), dtype=torch.int64, device=k.device)
+    if idx is not None:
+        idx = idx.to(dtype=torch.int32)
+        idx = idx if idx.stride(-1) == 1 else idx.contiguous()
+    a = _lib.EvictArgs(col=col.data_ptr(), sc_h=col.stride(0),
+                       idx=idx.data_ptr() if idx is not None and idx.numel() else None,
+                       si_h=idx.stride(0) if idx is not None else 0,
+                       budget=idx.shape[-1] if idx is not None else 0,
+                       k=k.data_ptr(), sk_h=k.stride(0), sk_t=k.stride(1),
+                       v=v.data_ptr(), sv_h=v.stride(0), sv_t=v.stride(1),
+                       out_k=out_k.data_ptr(), sok_h=out_k.stride(0), sok_t=out_k.stride(1),
+                       out_v=out_v.data_ptr(), sov_h=out_v.stride(0), sov_t=out_v.stride(1),
+                       out_pos=pos.data_ptr(), heads=H, kv_heads=Hk, n=n, d=d, sink=sink,
+                       window=window, keep=keep, pool=pool, pool_back=pool_back, dtype=_DT[k.dtype])
+    L_ = _lib.lib()
+    nbytes = C.c_size_t(0)
+    _lib.check(L_.bb_kv_evict_workspace_size(C.byref(a), C.byref(nbytes)), "kv_evict")
+    ws = _workspace(nbytes.value, k.device)
+    _lib.check(L_.bb_kv_evict(C.byref(a), _ptr(ws), nbytes.value, _stream(k)), "kv_evict")
+    return out_k, out_v, pos

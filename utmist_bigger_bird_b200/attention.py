@@ -168,47 +168,45 @@ class RDAttention(nn.Module):
                         scale=self.scaling)
         return out[None]
 
-    def evict_scores(self, q, k):
-        """[Hkv, n] key importance from the last ``evict_obs`` queries (reference 209-224)."""
-        n, g, hk = k.shape[-2], self.groups, self.num_kv_heads
+    def _evict_col(self, q, k):
+        """[H, n] exact-attention column scores of the last ``evict_obs`` queries: per query head,
+        the softmax over all keys of each of those queries (bf16/fp16 matmul output, then fp32),
+        pooled by mean or, with ``evict_obs_max``, max (reference 214-222). Computed by the routing
+        kernels with no sink/window columns and no top-k."""
+        n = k.shape[-2]
         r = min(self.evict_obs, n)
-        qa = q[0][:, n - r:, :].reshape(hk, g * r, self.head_dim)
-        qpos = torch.arange(n - r, n, device=q.device).repeat(g)
-        keypos = torch.arange(n, device=q.device)
-        out = torch.empty(hk, n, device=q.device, dtype=torch.float32)
-        for h in range(hk):
-            s = torch.matmul(qa[h], k[0, h].transpose(-1, -2)).float() * self.scaling
-            s.masked_fill_(keypos[None, :] > qpos[:, None], -float("inf"))
-            p = s.softmax(-1).view(g, r, n)
-            out[h] = (p.amax(1) if self.evict_obs_max else p.mean(1)).amax(0)
-        return out
+        qpos = torch.arange(n - r, n, device=q.device)
+        col = torch.empty(self.num_heads, n, device=q.device, dtype=torch.float32)
+        _ops.routes_(q[0], k[0], qpos, sink=0, window=0, budget=0, scaling=self.scaling,
+                     pool="max" if self.evict_obs_max else "mean", out_col=col)
+        return col
+
+    def evict_scores(self, q, k):
+        """[Hkv, n] key importance from the last ``evict_obs`` queries: exact softmax, mean (or
+        max) over those queries, max over each KV head's query group (reference 209-224)."""
+        hk, g = self.num_kv_heads, self.groups
+        return self._evict_col(q, k).view(hk, g, -1).amax(1)
 
     def evict(self, cache, q, k, v):
-        """Rewrite this layer's cache to sink + routed + window keys per KV head (reference
-        226-259)."""
-        n, d = k.shape[-2], k.shape[-1]
+        """Rewrite this layer's cache to sink + kept middle + window keys per KV head (reference
+        226-259): one native call computes the priorities (routed columns first, then the pooled
+        routing or exact-attention scores), selects the kept middle keys and gathers K/V."""
+        n = k.shape[-2]
         g, hk = self.groups, self.num_kv_heads
         idx, col, self._col = self.last_routes, self._col, None
         if self.layer_idx < self.evict_full_layers:
             self.kept = torch.arange(n, device=k.device)[None].expand(hk, -1)
             return
-        member = torch.zeros(self.num_heads, n, dtype=torch.bool, device=k.device)
-        member.scatter_(1, idx.long(), True)
-        score = self.evict_scores(q, k) if self.evict_obs else col.view(hk, g, n).amax(1)
-        if self.evict_pool > 1 or self.evict_pool_back:
-            score = forward_pool(score, self.evict_pool, self.evict_pool_back)
-        prio = member.view(hk, g, n).any(1).float() * 2 + score
+        if self.evict_obs:
+            col = self._evict_col(q, k)
         w = min(max(self.window, self.evict_window), n - self.sink)
-        prio[:, :self.sink] = -float("inf")
-        prio[:, n - w:] = -float("inf")
         extra = min(max(self.evict_keep, g * idx.shape[-1]) if self.evict_keep else g * idx.shape[-1],
                     n - self.sink - w)
-        sel = prio.topk(extra, dim=-1).indices.sort(-1).values
-        ar = torch.arange(n, device=k.device)
-        pos = torch.cat([ar[None, :self.sink].expand(hk, -1), sel, ar[None, n - w:].expand(hk, -1)], 1)
-        gi = pos[None, :, :, None].expand(1, hk, -1, d)
+        pool = self.evict_pool if (self.evict_pool > 1 or self.evict_pool_back) else 0
+        kk, vv, pos = _ops.kv_evict_(idx, col, k[0], v[0], sink=self.sink, window=w, keep=extra,
+                                     pool=pool, pool_back=self.evict_pool_back)
         layer = cache.layers[self.layer_idx]
-        layer.keys, layer.values = k.gather(2, gi), v.gather(2, gi)
+        layer.keys, layer.values = kk[None], vv[None]
         self.kept = pos
 
 

@@ -49,6 +49,8 @@ int rope_inplace(void* x, int dtype, int64_t B, int64_t H, int64_t T_, int64_t D
                  int64_t sct, cudaStream_t stream);
 int routes_workspace_size(const bb_routes_args* a, size_t* bytes);
 int routes(const bb_routes_args* a, void* ws, size_t ws_bytes, cudaStream_t stream);
+int kv_evict_workspace_size(const bb_evict_args* a, size_t* bytes);
+int kv_evict(const bb_evict_args* a, void* ws, size_t ws_bytes, cudaStream_t stream);
 int flash_workspace_size(const bb_flash_args* a, size_t* bytes);
 int flash(const bb_flash_args* a, void* ws, size_t ws_bytes, cudaStream_t stream);
 
@@ -176,6 +178,15 @@ int bb_routes_workspace_size(const bb_routes_args* a, size_t* bytes) {
 
 int bb_routes(const bb_routes_args* a, void* ws, size_t ws_bytes, bb_stream_t stream) {
   return bb::routes(a, ws, ws_bytes, bb::as_stream(stream));
+}
+
+int bb_kv_evict_workspace_size(const bb_evict_args* a, size_t* bytes) {
+  if (!bytes) return bb::fail(BB_ERR_ARG, "kv_evict: null bytes pointer");
+  return bb::kv_evict_workspace_size(a, bytes);
+}
+
+int bb_kv_evict(const bb_evict_args* a, void* ws, size_t ws_bytes, bb_stream_t stream) {
+  return bb::kv_evict(a, ws, ws_bytes, bb::as_stream(stream));
 }
 
 int bb_flash_workspace_size(const bb_flash_args* a, size_t* bytes) {

@@ -610,6 +610,16 @@ int launch_routes_d(const bb_routes_args* a, const RtPlan& pl, char* ws, cudaStr
 
 }  // namespace
 
+// The k largest of each of `rows` rows of n fp32 values, positions ascending (ties at the cut in
+// position order): the routing top-k, also used by KV eviction.
+int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, int32_t* out, int64_t so_h,
+                cudaStream_t stream) {
+  if (k <= 0 || rows <= 0) return BB_OK;
+  route_topk_kernel<<<(unsigned)rows, TK_THREADS, 0, stream>>>(vals, n, k, out, so_h);
+  BB_CHECK_LAUNCH("route_topk_kernel");
+  return BB_OK;
+}
+
 int routes_workspace_size(const bb_routes_args* a, size_t* bytes) {
   RtPlan pl;
   int st = plan_routes(a, &pl);
