@@ -317,6 +317,24 @@ def run_ours(args):
     route_bytes = per * n * d * 2 + H * min(cfg.n_route, n) * d * 2 + H * budget * 4
     route_gbs = route_bytes / (route_ms * 1e-3) / 1e9
 
+    # ---- KV eviction after the prefill (RDAttention.evict, default policy): priorities from the
+    # step's routes and routing column scores, the g*budget best middle keys, K/V gather. HBM-bound;
+    # algorithmic bytes = the column scores read + the kept K and V rows read and written.
+    col_buf = torch.empty(H, n, device=dev, dtype=torch.float32)
+    _ops.routes_(qr[0], kr[0], qpos, sink=cfg.sink, window=cfg.window, budget=budget, scaling=cfg.scaling,
+                 out_col=col_buf)
+    keep = min(g * budget, n - cfg.sink - cfg.window)
+
+    def evict():
+        _ops.kv_evict_(idx, col_buf, kr[0], v[0], sink=cfg.sink, window=cfg.window, keep=keep)
+
+    evict()
+    torch.cuda.synchronize(dev)
+    evict_ms = event_time(evict, reps, stream)
+    kept_rows = cfg.sink + keep + cfg.window
+    evict_bytes = H * n * 4 + 2 * 2 * per * kept_rows * d * 2
+    evict_gbs = evict_bytes / (evict_ms * 1e-3) / 1e9
+
     # ---- dense causal SDPA on the same inputs (the reference's comparator, attn_bench.py:47)
     import torch.nn.functional as F
     dense = lambda: F.scaled_dot_product_attention(qr, kr, v, is_causal=True, scale=cfg.scaling,  # noqa: E731
@@ -413,6 +431,9 @@ def run_ours(args):
         "routing": {"bound": "hbm", "ms": route_ms, "achieved_gbs": route_gbs, "peak_gbs": pk["hbm_gbs"],
                     "frac": route_gbs / pk["hbm_gbs"], "algorithmic_bytes": route_bytes},
         "exact_tail_ms": tail_ms,
+        "kv_evict": {"bound": "hbm", "ms": evict_ms, "kept_rows_per_kv_head": kept_rows,
+                     "achieved_gbs": evict_gbs, "peak_gbs": pk["hbm_gbs"], "frac": evict_gbs / pk["hbm_gbs"],
+                     "algorithmic_bytes": evict_bytes},
         "dense_sdpa": {"ms": dense_ms, "speedup_sparse_vs_dense": dense_ms / ms},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms": e2e_max, "h2d_bytes_per_step": h2d,
