@@ -15,6 +15,8 @@
  *                        (+ the in-place RoPE of forward, modal_rd/attention.py:121, when cos/sin given)
  *   bb_kv_evict          modal_rd/attention.py:226-259    RDAttention.evict(cache, q, k, v)
  *                        (+ forward_pool, modal_rd/attention.py:70-75)
+ *   bb_decode            kernels/bigger_bird_decode.py:67-107  bigger_bird_decode(q, k, v, indices, ...)
+ *   bb_decode_route      kernels/bigger_bird_route.py:80-115   pooled_probs / bigger_bird_route(q, k, k_route)
  */
 #ifndef BB_B200_H
 #define BB_B200_H
@@ -203,6 +205,46 @@ typedef struct {
 
 BB_API int bb_kv_evict_workspace_size(const bb_evict_args* a, size_t* bytes);
 BB_API int bb_kv_evict(const bb_evict_args* a, void* workspace, size_t workspace_bytes, bb_stream_t stream);
+
+/*
+ * Decode (one new query token per head) over a KV cache of capacity `cap`, of which the first n
+ * keys are valid: n is the host value `n`, or, when `n_dev` is non-NULL, a device int64 read at
+ * run time (so a captured CUDA graph stays valid while the cache grows).
+ *
+ * bb_decode (bigger_bird_decode, kernels/bigger_bird_decode.py:67-107): each query head attends to
+ * the front keys [0, front), the last `window` keys [n - window, n) and its routed keys
+ * idx[route row, :] (route rows = Hkv for pooled routes shared by a KV head's query heads, or H for
+ * per-head routes; entries outside [0, n) are skipped; routed keys must lie in [front, n - window)
+ * and be unique per row). Split-K flash decoding: P is rounded to the cache dtype before P.V.
+ * out: [H, d] in the q dtype. route_k = 0: no routed keys (front = 0, window = cap: dense decoding).
+ *
+ * bb_decode_route (pooled_probs / bigger_bird_route, kernels/bigger_bird_route.py:80-115): per KV
+ * head, the probability of every cached key under each query head's softmax over the first n
+ * keys, averaged over the KV head's query heads; -1 outside [front, n - window). out_probs (may be
+ * NULL): [Hkv, cap] fp32; out_idx (may be NULL): [Hkv, route_k] int32, the route_k most probable
+ * keys, positions ascending.
+ */
+typedef struct {
+  const void* q; int64_t sq_h;              /* [H, d], innermost stride 1 */
+  const void* k; int64_t sk_h, sk_t;        /* [Hkv, cap, d] */
+  const void* v; int64_t sv_h, sv_t;        /* [Hkv, cap, d] (bb_decode only) */
+  const int32_t* idx; int64_t si_r;         /* [route_rows, route_k] (bb_decode) */
+  int64_t route_rows, route_k;              /* bb_decode_route: route_k = keys to select */
+  int64_t n; const int64_t* n_dev;          /* valid keys: n, or *n_dev when n_dev != NULL */
+  int64_t cap, heads, kv_heads, d;
+  int64_t front, window;
+  float scale;
+  int64_t splits;                           /* 0: enough chunks for ~4 CTAs per SM */
+  void* out; int64_t so_h;                  /* bb_decode: [H, d] */
+  float* out_probs;                         /* bb_decode_route: [Hkv, cap] or NULL */
+  int32_t* out_idx; int64_t so_i;           /* bb_decode_route: [Hkv, route_k] or NULL */
+  int dtype;                                /* BB_F16 / BB_BF16 */
+} bb_decode_args;
+
+BB_API int bb_decode_workspace_size(const bb_decode_args* a, size_t* bytes);
+BB_API int bb_decode(const bb_decode_args* a, void* workspace, size_t workspace_bytes, bb_stream_t stream);
+BB_API int bb_decode_route_workspace_size(const bb_decode_args* a, size_t* bytes);
+BB_API int bb_decode_route(const bb_decode_args* a, void* workspace, size_t workspace_bytes, bb_stream_t stream);
 
 #ifdef __cplusplus
 }

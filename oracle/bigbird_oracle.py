@@ -23,6 +23,12 @@ What it restates (paths inside the reference project derkychen/utmist-bigger-bir
                         query rows so long sequences stay tractable.
 * ``sparse_prefill`` -- ``modal_rd/attention.py:176-206`` (routes, optional ``vertical_scope``
                         groups, main pass, exact tail overwriting the last ``exact_tail`` rows).
+* ``decode``         -- ``kernels/bigger_bird_decode.py:21-107``: one query per head over the virtual
+                        key list front | window | routed (positions outside [0, n) skipped; a key
+                        listed twice counts twice, as in the kernel), exact softmax in fp32.
+* ``pooled_probs``   -- ``kernels/bigger_bird_route.py:24-106``: per-head base-2 softmax of the
+                        fp32 scores over the first n keys, mean over the KV head's query heads, -1
+                        outside [front, n - window).
 * ``forward_pool`` / ``evict_positions`` -- ``modal_rd/attention.py:70-75`` and ``:226-259``
                         (``RDAttention.evict``): routed columns first, then the group-max (pooled)
                         column scores, sink and kept window excluded, top-``keep`` sorted; the
@@ -40,7 +46,7 @@ import numpy as np
 __all__ = [
     "bf16_round", "f16_round", "rounder", "rope", "vertical_budget", "route_query_positions",
     "route_scores", "routes", "topk_sorted", "route_sets_match", "flash", "sparse_prefill",
-    "forward_pool", "evict_positions",
+    "forward_pool", "evict_positions", "decode", "pooled_probs",
 ]
 
 
@@ -346,3 +352,50 @@ def evict_positions(idx, col, *, kv_heads, sink, window, evict_keep=0, evict_win
     ar = np.arange(n, dtype=np.int64)
     pos = np.concatenate([np.tile(ar[:sink], (hk, 1)), sel, np.tile(ar[n - w:], (hk, 1))], axis=1)
     return pos, prio
+
+
+# ----------------------------------------------------------------------------- decode
+def decode(q, k, v, indices, *, front, window, scale, n=None):
+    """``bigger_bird_decode`` (``kernels/bigger_bird_decode.py:67-107``) in fp32: q [H, D], k/v
+    [Hkv, cap, D], indices [Hkv or H, R] -> [H, D]."""
+    q = np.asarray(q, dtype=np.float32)
+    k = np.asarray(k, dtype=np.float32)
+    v = np.asarray(v, dtype=np.float32)
+    idx = np.asarray(indices, dtype=np.int64).reshape(np.asarray(indices).shape[0], -1)
+    H, D = q.shape
+    hk, cap, _ = k.shape
+    g = H // hk
+    n = cap if n is None else int(n)
+    pooled = idx.shape[0] == hk and hk != H
+    out = np.zeros((H, D), dtype=np.float32)
+    for h in range(H):
+        kv = h // g
+        row = idx[kv] if pooled else idx[h]
+        pos = np.concatenate([np.arange(front), n - window + np.arange(window), row])
+        pos = pos[(pos >= 0) & (pos < n)]
+        s = (k[kv, pos].astype(np.float64) @ q[h].astype(np.float64)) * scale
+        if s.size == 0:
+            out[h] = np.nan
+            continue
+        p = np.exp(s - s.max())
+        out[h] = ((p / p.sum()) @ v[kv, pos].astype(np.float64)).astype(np.float32)
+    return out
+
+
+def pooled_probs(q, k, *, front, window, scale, n=None):
+    """``pooled_probs`` (``kernels/bigger_bird_route.py:80-106``): [Hkv, cap] fp32."""
+    q = np.asarray(q, dtype=np.float32)
+    k = np.asarray(k, dtype=np.float32)
+    H, D = q.shape
+    hk, cap, _ = k.shape
+    g = H // hk
+    n = cap if n is None else int(n)
+    out = np.full((hk, cap), -1.0, dtype=np.float32)
+    for kv in range(hk):
+        s = (q[kv * g:(kv + 1) * g].astype(np.float64) @ k[kv, :n].astype(np.float64).T) * scale
+        e = np.exp(s - s.max(-1, keepdims=True))
+        p = (e / e.sum(-1, keepdims=True)).mean(0)
+        keep = np.zeros(cap, dtype=bool)
+        keep[front:max(front, n - window)] = True
+        out[kv, :n] = np.where(keep[:n], p, -1.0)
+    return out

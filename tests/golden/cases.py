@@ -130,6 +130,25 @@ EVICT_CONFIGS = {
 }
 
 
+# Decode (one new token): pinned through the reference's own functions that run on the CPU. A
+# one-query decode over front | window | routed equals bigger_bird_flash_ref for the last query
+# row with the same routes; in fp32, pooled_probs equals the mean over a KV head's query heads of
+# RDAttention.routes' column scores with n_route=1 (the same masks).
+DECODE_SHAPE = dict(H=8, hk=2, d=32, n=300, front=8, window=64, R=24)
+
+
+def decode_inputs():
+    s = DECODE_SHAPE
+    g = torch.Generator().manual_seed(11)
+    q = torch.randn(1, s["H"], s["n"], s["d"], generator=g)
+    k = torch.randn(1, s["hk"], s["n"], s["d"], generator=g)
+    v = torch.randn(1, s["hk"], s["n"], s["d"], generator=g)
+    lo, hi = s["front"], s["n"] - s["window"]
+    pooled = torch.stack([torch.randperm(hi - lo, generator=g)[:s["R"]] + lo for _ in range(s["hk"])])
+    pooled = pooled.sort(-1).values.to(torch.int32)
+    return q, k, v, pooled
+
+
 def config1_rows(n):
     return torch.cat([torch.linspace(0, n - 300, 12).long(), torch.arange(n - 258, n - 254),
                       torch.arange(n - 4, n)])

@@ -155,6 +155,24 @@ def gen_evict():
     return out
 
 
+def gen_decode():
+    """One-token decode and decode routing through the reference's CPU functions (fp32)."""
+    s = cases.DECODE_SHAPE
+    q, k, v, pooled = cases.decode_inputs()
+    n, H, hk, d = s["n"], s["H"], s["hk"], s["d"]
+    g = H // hk
+    per_head = pooled.repeat_interleave(g, 0)[:, None, :]       # [H, 1, R]
+    o = bigger_bird_flash_ref(q[0, :, n - 1:], k[0], v[0], per_head, front=s["front"], window=s["window"],
+                              num_heads=H, kv_groups=g, scale=d ** -0.5)
+    out = dict(check=cases.checksum(q, k, v), pooled=pooled.numpy(), decode_out=f32(o[:, 0]))
+    attn = ref_attn.RDAttention(base(H, hk, d), kv_evict=True, sink=s["front"], window=s["window"],
+                                vertical=s["R"], n_route=1)
+    with torch.inference_mode():
+        attn.routes(q, k)
+    out["route_col"] = attn._col.numpy()                          # [H, n], sink/window columns -1
+    return {"decode": out}
+
+
 def save(name, groups):
     flat = {}
     for key, rec in groups.items():
@@ -171,3 +189,4 @@ if __name__ == "__main__":
     save("prefill", gen_prefill())
     save("config1", gen_config1())
     save("evict", gen_evict())
+    save("decode", gen_decode())

@@ -32,7 +32,8 @@ def test_library_exports_every_declared_symbol():
 
 def test_struct_layouts_match_header(tmp_path):
     structs = {"bb_routes_args": _lib.RoutesArgs, "bb_flash_args": _lib.FlashArgs,
-               "bb_prefill_args": _lib.PrefillArgs, "bb_evict_args": _lib.EvictArgs}
+               "bb_prefill_args": _lib.PrefillArgs, "bb_evict_args": _lib.EvictArgs,
+               "bb_decode_args": _lib.DecodeArgs}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void) {"]
     for cname, py in structs.items():
         lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
@@ -162,3 +163,24 @@ def test_kv_evict_workspace_size():
     assert L.bb_kv_evict_workspace_size(C.byref(a), C.byref(nbytes)) == 0
     cells = 8 * 131072
     assert nbytes.value >= cells * (1 + 4 + 4) + 8 * 2048 * 4
+
+
+@pytest.mark.parametrize("kw,fn,msg", [
+    (dict(dtype=_lib.BB_F32), "bb_decode_workspace_size", "fp16 or bf16"),
+    (dict(heads=7), "bb_decode_workspace_size", "multiple of kv_heads"),
+    (dict(d=136), "bb_decode_workspace_size", "head_dim"),
+    (dict(n=5000), "bb_decode_workspace_size", "n must lie"),
+    (dict(route_rows=3, route_k=8), "bb_decode_workspace_size", "pooled"),
+    (dict(heads=64, kv_heads=2), "bb_decode_workspace_size", "query heads per KV head"),
+    (dict(route_k=5000), "bb_decode_route_workspace_size", "k_route"),
+])
+def test_decode_host_validation(kw, fn, msg):
+    """bb_decode / bb_decode_route argument checks run on the host (no device needed)."""
+    L = _lib.lib()
+    args = dict(heads=32, kv_heads=8, d=128, cap=4096, n=4096, front=64, window=512, route_rows=8, route_k=0,
+                scale=0.088, dtype=_lib.BB_BF16)
+    args.update(kw)
+    a = _lib.DecodeArgs(**args)
+    nbytes = C.c_size_t(0)
+    assert getattr(L, fn)(C.byref(a), C.byref(nbytes)) != 0
+    assert msg in L.bb_last_error().decode()

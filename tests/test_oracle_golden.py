@@ -179,3 +179,31 @@ def test_oracle_forward_pool_spans():
     pooled = orc.forward_pool(score, 3, back=4)
     assert (pooled[0, 6:13] == 1).all() and (pooled[0, :6] == 0).all() and (pooled[0, 13:] == 0).all()
     assert (orc.forward_pool(score, 0, back=2)[0, 8:11] == 1).all()
+
+
+def test_oracle_decode_matches_reference(golden):
+    """One-token decode (kernels/bigger_bird_decode.py) through the oracle equals the reference's
+    bigger_bird_flash_ref on the last query row with the same (pooled) routes."""
+    g = golden("decode")["decode"]
+    s = cases.DECODE_SHAPE
+    q, k, v, pooled = cases.decode_inputs()
+    np.testing.assert_allclose(g["check"], cases.checksum(q, k, v), rtol=0, atol=0)
+    n = s["n"]
+    got = orc.decode(np32(q[0, :, n - 1]), np32(k[0]), np32(v[0]), pooled.numpy(), front=s["front"],
+                     window=s["window"], scale=s["d"] ** -0.5)
+    np.testing.assert_allclose(got, g["decode_out"], rtol=1e-5, atol=1e-5)
+
+
+def test_oracle_pooled_probs_matches_reference(golden):
+    """pooled_probs (kernels/bigger_bird_route.py) through the oracle equals the group mean of the
+    reference's RDAttention.routes column scores for the last query (fp32, same masks)."""
+    g = golden("decode")["decode"]
+    s = cases.DECODE_SHAPE
+    q, k, _, _ = cases.decode_inputs()
+    n, hk = s["n"], s["hk"]
+    got = orc.pooled_probs(np32(q[0, :, n - 1]), np32(k[0]), front=s["front"], window=s["window"],
+                           scale=s["d"] ** -0.5)
+    col = g["route_col"].reshape(hk, -1, n)
+    want = col.mean(1)
+    want[col[:, 0] == -1] = -1
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-9)

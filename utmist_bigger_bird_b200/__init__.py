@@ -8,5 +8,8 @@ The compute runs in ``libbb_b200.so`` (C ABI: include/bb_b200.h); build it with
 """
 from .attention import RDAttention, forward_pool, install, rope_inplace, vertical_budget  # noqa: F401
 from .bigger_bird_flash import bigger_bird_flash  # noqa: F401
+from .bigger_bird_decode import bigger_bird_decode  # noqa: F401
+from .bigger_bird_route import bigger_bird_route, pooled_probs  # noqa: F401
 
-__all__ = ["RDAttention", "install", "rope_inplace", "vertical_budget", "forward_pool", "bigger_bird_flash"]
+__all__ = ["RDAttention", "install", "rope_inplace", "vertical_budget", "forward_pool", "bigger_bird_flash",
+           "bigger_bird_decode", "bigger_bird_route", "pooled_probs"]

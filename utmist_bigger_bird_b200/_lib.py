@@ -74,6 +74,23 @@ class EvictArgs(C.Structure):
                 ("dtype", C.c_int)]
 
 
+class DecodeArgs(C.Structure):
+    _fields_ = [("q", vp), ("sq_h", i64),
+                ("k", vp), ("sk_h", i64), ("sk_t", i64),
+                ("v", vp), ("sv_h", i64), ("sv_t", i64),
+                ("idx", vp), ("si_r", i64),
+                ("route_rows", i64), ("route_k", i64),
+                ("n", i64), ("n_dev", vp),
+                ("cap", i64), ("heads", i64), ("kv_heads", i64), ("d", i64),
+                ("front", i64), ("window", i64),
+                ("scale", f32),
+                ("splits", i64),
+                ("out", vp), ("so_h", i64),
+                ("out_probs", vp),
+                ("out_idx", vp), ("so_i", i64),
+                ("dtype", C.c_int)]
+
+
 EXPORTS = {
     "bb_last_error": (C.c_char_p, []),
     "bb_abi_version": (C.c_int, []),
@@ -89,6 +106,10 @@ EXPORTS = {
     "bb_sparse_prefill": (C.c_int, [C.POINTER(PrefillArgs), vp, C.c_size_t, vp]),
     "bb_kv_evict_workspace_size": (C.c_int, [C.POINTER(EvictArgs), C.POINTER(C.c_size_t)]),
     "bb_kv_evict": (C.c_int, [C.POINTER(EvictArgs), vp, C.c_size_t, vp]),
+    "bb_decode_workspace_size": (C.c_int, [C.POINTER(DecodeArgs), C.POINTER(C.c_size_t)]),
+    "bb_decode": (C.c_int, [C.POINTER(DecodeArgs), vp, C.c_size_t, vp]),
+    "bb_decode_route_workspace_size": (C.c_int, [C.POINTER(DecodeArgs), C.POINTER(C.c_size_t)]),
+    "bb_decode_route": (C.c_int, [C.POINTER(DecodeArgs), vp, C.c_size_t, vp]),
 }
 
 _lib = None

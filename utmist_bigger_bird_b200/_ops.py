@@ -177,3 +177,63 @@ def kv_evict_(idx: torch.Tensor | None, col: torch.Tensor, k: torch.Tensor, v: t
     ws = _workspace(nbytes.value, k.device)
     _lib.check(L_.bb_kv_evict(C.byref(a), _ptr(ws), nbytes.value, _stream(k)), "kv_evict")
     return out_k, out_v, pos
+
+
+def _n_arg(n, cap, device):
+    """(host n, device pointer or None, keep-alive tensor) for a cache length given as None, an int
+    or a 1-element GPU integer tensor (read by the kernels at run time)."""
+    if n is None:
+        return cap, None, None
+    if isinstance(n, torch.Tensor):
+        t = n.reshape(-1)[:1]
+        if t.dtype != torch.int64 or not t.is_contiguous() or t.device != device:
+            t = t.to(device=device, dtype=torch.int64).contiguous()
+        return cap, t.data_ptr(), t
+    return int(n), None, None
+
+
+def decode_(q, k, v, idx, out, *, front, window, scale, n=None, splits=0):
+    """One-token sparse decode: q [H, d], k/v [Hkv, cap, d] (cache views), idx [Hkv or H, R] int32
+    (or None), out [H, d]. ``n``: cache length (None = cap, int, or 1-element GPU tensor)."""
+    H, d = q.shape
+    hk, cap, _ = k.shape
+    if k.stride(-1) != 1 or v.stride(-1) != 1 or q.stride(-1) != 1 or out.stride(-1) != 1:
+        raise ValueError("decode: innermost strides must be 1")
+    n_host, n_ptr, keep = _n_arg(n, cap, q.device)
+    R = idx.shape[1] if idx is not None else 0
+    a = _lib.DecodeArgs(q=q.data_ptr(), sq_h=q.stride(0), k=k.data_ptr(), sk_h=k.stride(0), sk_t=k.stride(1),
+                        v=v.data_ptr(), sv_h=v.stride(0), sv_t=v.stride(1),
+                        idx=idx.data_ptr() if R else None, si_r=idx.stride(0) if R else 0,
+                        route_rows=idx.shape[0] if idx is not None else hk, route_k=R,
+                        n=n_host, n_dev=n_ptr, cap=cap, heads=H, kv_heads=hk, d=d, front=front, window=window,
+                        scale=scale, splits=splits or 0, out=out.data_ptr(), so_h=out.stride(0),
+                        dtype=_DT[q.dtype])
+    L = _lib.lib()
+    nbytes = C.c_size_t(0)
+    _lib.check(L.bb_decode_workspace_size(C.byref(a), C.byref(nbytes)), "bigger_bird_decode")
+    ws = _workspace(nbytes.value, q.device)
+    _lib.check(L.bb_decode(C.byref(a), _ptr(ws), nbytes.value, _stream(q)), "bigger_bird_decode")
+    del keep
+    return out
+
+
+def decode_route_(q, k, *, front, window, scale, n=None, k_route=0, probs=None, idx_out=None, splits=0):
+    """Decode routing: pooled probabilities [Hkv, cap] fp32 into ``probs`` (optional) and the
+    ``k_route`` most probable keys per KV head into ``idx_out`` [Hkv, k_route] int32 (optional)."""
+    H, d = q.shape
+    hk, cap, _ = k.shape
+    if k.stride(-1) != 1 or q.stride(-1) != 1:
+        raise ValueError("decode_route: innermost strides must be 1")
+    n_host, n_ptr, keep = _n_arg(n, cap, q.device)
+    a = _lib.DecodeArgs(q=q.data_ptr(), sq_h=q.stride(0), k=k.data_ptr(), sk_h=k.stride(0), sk_t=k.stride(1),
+                        route_rows=hk, route_k=k_route, n=n_host, n_dev=n_ptr, cap=cap, heads=H, kv_heads=hk,
+                        d=d, front=front, window=window, scale=scale, splits=splits or 0,
+                        out_probs=probs.data_ptr() if probs is not None else None,
+                        out_idx=idx_out.data_ptr() if idx_out is not None else None,
+                        so_i=idx_out.stride(0) if idx_out is not None else 0, dtype=_DT[q.dtype])
+    L = _lib.lib()
+    nbytes = C.c_size_t(0)
+    _lib.check(L.bb_decode_route_workspace_size(C.byref(a), C.byref(nbytes)), "bigger_bird_route")
+    ws = _workspace(nbytes.value, q.device)
+    _lib.check(L.bb_decode_route(C.byref(a), _ptr(ws), nbytes.value, _stream(q)), "bigger_bird_route")
+    del keep

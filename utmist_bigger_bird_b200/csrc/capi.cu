@@ -51,6 +51,10 @@ int routes_workspace_size(const bb_routes_args* a, size_t* bytes);
 int routes(const bb_routes_args* a, void* ws, size_t ws_bytes, cudaStream_t stream);
 int kv_evict_workspace_size(const bb_evict_args* a, size_t* bytes);
 int kv_evict(const bb_evict_args* a, void* ws, size_t ws_bytes, cudaStream_t stream);
+int decode_workspace_size(const bb_decode_args* a, size_t* bytes);
+int decode(const bb_decode_args* a, void* ws, size_t ws_bytes, cudaStream_t stream);
+int decode_route_workspace_size(const bb_decode_args* a, size_t* bytes);
+int decode_route(const bb_decode_args* a, void* ws, size_t ws_bytes, cudaStream_t stream);
 int flash_workspace_size(const bb_flash_args* a, size_t* bytes);
 int flash(const bb_flash_args* a, void* ws, size_t ws_bytes, cudaStream_t stream);
 
@@ -187,6 +191,24 @@ int bb_kv_evict_workspace_size(const bb_evict_args* a, size_t* bytes) {
 
 int bb_kv_evict(const bb_evict_args* a, void* ws, size_t ws_bytes, bb_stream_t stream) {
   return bb::kv_evict(a, ws, ws_bytes, bb::as_stream(stream));
+}
+
+int bb_decode_workspace_size(const bb_decode_args* a, size_t* bytes) {
+  if (!bytes) return bb::fail(BB_ERR_ARG, "decode: null bytes pointer");
+  return bb::decode_workspace_size(a, bytes);
+}
+
+int bb_decode(const bb_decode_args* a, void* ws, size_t ws_bytes, bb_stream_t stream) {
+  return bb::decode(a, ws, ws_bytes, bb::as_stream(stream));
+}
+
+int bb_decode_route_workspace_size(const bb_decode_args* a, size_t* bytes) {
+  if (!bytes) return bb::fail(BB_ERR_ARG, "decode_route: null bytes pointer");
+  return bb::decode_route_workspace_size(a, bytes);
+}
+
+int bb_decode_route(const bb_decode_args* a, void* ws, size_t ws_bytes, bb_stream_t stream) {
+  return bb::decode_route(a, ws, ws_bytes, bb::as_stream(stream));
 }
 
 int bb_flash_workspace_size(const bb_flash_args* a, size_t* bytes) {
