@@ -225,6 +225,95 @@ def event_time(fn, reps, stream):
     return s.elapsed_time(e) / reps
 
 
+def flushed_time(fn, reps, stream, scrub):
+    """Mean device time of fn over reps calls, each after a read of ``scrub`` (larger than L2) so
+    that a working set smaller than L2 is read from HBM every call; the scrub is outside the timing.
+    A read, not a write: a written scrub would leave L2 full of dirty lines whose write-back the
+    timed call would pay for.
+    fn is captured once into a CUDA graph and replayed, the way a serving loop runs these short
+    calls, so that the host's Python time does not open gaps inside the timed region."""
+    side = torch.cuda.Stream(stream.device)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        fn()
+        fn()
+    stream.wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        fn()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for s, e in ev:
+        scrub.sum()
+        s.record(stream)
+        graph.replay()
+        e.record(stream)
+    ev[-1][1].synchronize()
+    del graph
+    return sum(s.elapsed_time(e) for s, e in ev) / reps
+
+
+def side_paths(cfg, qr, kr, v, idx, qpos, budget, dev, stream, reps, pk, parts=("evict", "decode")):
+    """KV eviction and decode on this rank's post-RoPE cache (kr, v) and prefill routes (idx);
+    returns their JSON objects (None for a part not asked for)."""
+    from utmist_bigger_bird_b200 import _ops
+    per, H, n, d = kr.shape[1], qr.shape[1], kr.shape[2], kr.shape[3]
+    g = H // per
+    scrub = torch.ones(64 << 20, device=dev, dtype=torch.float32)  # 256 MB, twice L2
+    evict_line = decode_line = None
+    if "evict" in parts:
+        # ---- KV eviction after the prefill (RDAttention.evict, default policy): priorities from the
+        # step's routes and routing column scores, the g*budget best middle keys, K/V gather. HBM-bound;
+        # algorithmic bytes = the column scores read + the kept K and V rows read and written. Its working
+        # set (and the sparse decode's) fits in L2, so these are timed with L2 scrubbed before each call.
+        col_buf = torch.empty(H, n, device=dev, dtype=torch.float32)
+        _ops.routes_(qr[0], kr[0], qpos, sink=cfg.sink, window=cfg.window, budget=budget, scaling=cfg.scaling,
+                     out_col=col_buf)
+        keep = min(g * budget, n - cfg.sink - cfg.window)
+
+        def evict():
+            _ops.kv_evict_(idx, col_buf, kr[0], v[0], sink=cfg.sink, window=cfg.window, keep=keep)
+
+        evict()
+        torch.cuda.synchronize(dev)
+        evict_ms = flushed_time(evict, reps, stream, scrub)
+        kept_rows = cfg.sink + keep + cfg.window
+        evict_bytes = H * n * 4 + 2 * 2 * per * kept_rows * d * 2
+        evict_gbs = evict_bytes / (evict_ms * 1e-3) / 1e9
+        evict_line = {"bound": "hbm", "ms": evict_ms, "kept_rows_per_kv_head": kept_rows, "achieved_gbs": evict_gbs,
+                      "peak_gbs": pk["hbm_gbs"], "frac": evict_gbs / pk["hbm_gbs"], "algorithmic_bytes": evict_bytes}
+
+    if "decode" in parts:
+        # ---- decode of one new token per head over this rank's cache (n keys): decode routing
+        # (pooled probabilities + top-budget per KV head), sparse split-K decoding over front | window |
+        # pooled routes, and dense flash-decoding over all n keys. HBM-bound; algorithmic bytes = the
+        # K (and V) rows each one must read.
+        from utmist_bigger_bird_b200 import bigger_bird_decode, bigger_bird_route
+        qd = qr[0, :, n - 1].contiguous()
+        droute = lambda: bigger_bird_route(qd, kr[0], budget, front=cfg.sink, window=cfg.window,  # noqa: E731
+                                           scale=cfg.scaling)
+        didx = droute()
+        dsparse = lambda: bigger_bird_decode(qd, kr[0], v[0], didx, front=cfg.sink, window=cfg.window,  # noqa: E731
+                                             scale=cfg.scaling)
+        no_routes = didx[:, :0]
+        ddense = lambda: bigger_bird_decode(qd, kr[0], v[0], no_routes, front=0, window=n,  # noqa: E731
+                                            scale=cfg.scaling)
+        for fn in (dsparse, ddense):
+            fn()
+        torch.cuda.synchronize(dev)
+        dec = {}
+        for name, fn, nbytes in (("route", droute, per * n * d * 2),
+                                 ("sparse", dsparse, 2 * per * (cfg.sink + cfg.window + budget) * d * 2),
+                                 ("dense", ddense, 2 * per * n * d * 2)):
+            t = flushed_time(fn, reps * 3, stream, scrub)
+            gbs = nbytes / (t * 1e-3) / 1e9
+            dec[name] = {"ms": t, "algorithmic_bytes": nbytes, "achieved_gbs": gbs, "frac": gbs / pk["hbm_gbs"]}
+        decode_line = dict(dec, bound="hbm", peak_gbs=pk["hbm_gbs"],
+                           config=f"one token per head over the rank's {n}-key cache: route = pooled probabilities + "
+                                  f"top-{budget} per KV head; sparse = front {cfg.sink} | window {cfg.window} | "
+                                  f"{budget} pooled routes; dense = all keys")
+    return evict_line, decode_line
+
+
 def run_ours(args):
     import torch.distributed as dist
 
@@ -317,23 +406,7 @@ def run_ours(args):
     route_bytes = per * n * d * 2 + H * min(cfg.n_route, n) * d * 2 + H * budget * 4
     route_gbs = route_bytes / (route_ms * 1e-3) / 1e9
 
-    # ---- KV eviction after the prefill (RDAttention.evict, default policy): priorities from the
-    # step's routes and routing column scores, the g*budget best middle keys, K/V gather. HBM-bound;
-    # algorithmic bytes = the column scores read + the kept K and V rows read and written.
-    col_buf = torch.empty(H, n, device=dev, dtype=torch.float32)
-    _ops.routes_(qr[0], kr[0], qpos, sink=cfg.sink, window=cfg.window, budget=budget, scaling=cfg.scaling,
-                 out_col=col_buf)
-    keep = min(g * budget, n - cfg.sink - cfg.window)
-
-    def evict():
-        _ops.kv_evict_(idx, col_buf, kr[0], v[0], sink=cfg.sink, window=cfg.window, keep=keep)
-
-    evict()
-    torch.cuda.synchronize(dev)
-    evict_ms = event_time(evict, reps, stream)
-    kept_rows = cfg.sink + keep + cfg.window
-    evict_bytes = H * n * 4 + 2 * 2 * per * kept_rows * d * 2
-    evict_gbs = evict_bytes / (evict_ms * 1e-3) / 1e9
+    evict_line, decode_line = side_paths(cfg, qr, kr, v, idx, qpos, budget, dev, stream, reps, pk)
 
     # ---- dense causal SDPA on the same inputs (the reference's comparator, attn_bench.py:47)
     import torch.nn.functional as F
@@ -431,9 +504,8 @@ def run_ours(args):
         "routing": {"bound": "hbm", "ms": route_ms, "achieved_gbs": route_gbs, "peak_gbs": pk["hbm_gbs"],
                     "frac": route_gbs / pk["hbm_gbs"], "algorithmic_bytes": route_bytes},
         "exact_tail_ms": tail_ms,
-        "kv_evict": {"bound": "hbm", "ms": evict_ms, "kept_rows_per_kv_head": kept_rows,
-                     "achieved_gbs": evict_gbs, "peak_gbs": pk["hbm_gbs"], "frac": evict_gbs / pk["hbm_gbs"],
-                     "algorithmic_bytes": evict_bytes},
+        "kv_evict": evict_line,
+        "decode": decode_line,
         "dense_sdpa": {"ms": dense_ms, "speedup_sparse_vs_dense": dense_ms / ms},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms": e2e_max, "h2d_bytes_per_step": h2d,
@@ -445,6 +517,30 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
 
 
+def run_part(args):
+    """One side path alone on one GPU (``--part decode`` or ``--part evict``), at the config's full
+    size: the layer's post-RoPE cache and prefill routes, then that part's timing as one JSON line.
+    Used for focused profiling of those kernels."""
+    from utmist_bigger_bird_b200 import _ops
+    from utmist_bigger_bird_b200.attention import route_query_positions, vertical_budget
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = CONFIGS[args.config]
+    n = cfg.n
+    q, k, v, cos, sin, _ = (t.to(dev) for t in make_layer(cfg, kv_heads=list(range(cfg.kv_heads))))
+    _ops.rope_inplace_(q, cos, sin)
+    _ops.rope_inplace_(k, cos, sin)
+    budget = min(vertical_budget(n, cfg.vertical, 0.0), max(0, n - cfg.sink - cfg.window))
+    qpos = route_query_positions(n, min(cfg.n_route, n), "last", cfg.sink, cfg.window, dev)
+    idx = _ops.routes_(q[0], k[0], qpos, sink=cfg.sink, window=cfg.window, budget=budget, scaling=cfg.scaling)
+    pk, _ = peaks()
+    stream = torch.cuda.current_stream(dev)
+    reps = max(3, min(args.steps, 10))
+    evict_line, decode_line = side_paths(cfg, q, k, v, idx, qpos, budget, dev, stream, reps, pk, parts=(args.part,))
+    print(json.dumps({"part": args.part, "workload": cfg.name, "kv_evict": evict_line, "decode": decode_line}),
+          flush=True)
+
+
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -453,8 +549,12 @@ def main():
     p.add_argument("--config", default="config2", choices=sorted(CONFIGS))
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    p.add_argument("--part", default="all", choices=["all", "decode", "evict"],
+                   help="time one side path alone (1 GPU) instead of the full benchmark")
     args = p.parse_args()
-    if args.impl == "reference":
+    if args.part != "all":
+        run_part(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -34,7 +34,7 @@ def np32(t):
 
 
 @pytest.mark.parametrize("mode", ["pooled", "per_head"])
-@pytest.mark.parametrize("d", [128, 64])
+@pytest.mark.parametrize("d", [128, 64, 96, 32])
 def test_decode_matches_oracle(mode, d):
     from utmist_bigger_bird_b200 import bigger_bird_decode
     H, hk, cap, front, window, R = 32, 8, 32768, 64, 4096, 512

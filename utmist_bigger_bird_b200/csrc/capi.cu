@@ -161,12 +161,14 @@ uint64_t bb_kernel_launches(void) { return bb::g_launches.load(std::memory_order
 
 int bb_device_fault(int* code) {
   if (!code) return bb::fail(BB_ERR_ARG, "device_fault: null pointer");
-  int a = 0, b = 0;
+  int a = 0, b = 0, c = 0;
   int st = bb::flash_fault_take(&a);
   if (st != BB_OK) return st;
   st = bb::routes_fault_take(&b);
   if (st != BB_OK) return st;
-  *code = a ? a : b;
+  st = bb::decode_fault_take(&c);
+  if (st != BB_OK) return st;
+  *code = a ? a : (b ? b : c);
   return BB_OK;
 }
 

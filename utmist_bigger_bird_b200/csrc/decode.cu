@@ -12,13 +12,19 @@
 //   droute_pool_kernel     pass 2 (:56-77): merged statistics, probabilities averaged over the group,
 //                          -1 outside [front, n - window).
 //
-// Keys and values are read in place from the cache (any head/row strides, rows 16-byte aligned).
-// The cache length can come from a device int64 (`n_dev`), so a captured CUDA graph stays valid as
+// Keys and values are read in place from the cache (any head/row strides, rows 16-byte aligned):
+// each cache row is one bulk copy (cp.async.bulk, d * 2 bytes) into a padded shared-memory row,
+// completing on the stage's mbarrier, so gathering routed rows costs one instruction a row. The
+// cache length can come from a device int64 (`n_dev`), so a captured CUDA graph stays valid as
 // the cache grows inside a fixed-capacity buffer. All of it is bound by HBM (each cache row is read
-// once per route group); the dot products run on CUDA cores.
+// once per route group); the dot products run on the tensor cores (mma.sync m16n8k16, the group's
+// query heads as the 16 rows), so the instruction stream stays far below the copy time. Every
+// wait on a stage is bounded (about 2 s): a CTA that gives up records a fault code (40, 41) for
+// bb_device_fault, drains its copies in flight and returns.
 #include <algorithm>
+#include <climits>
 
-#include "bb_common.cuh"
+#include "tc_common.cuh"
 
 namespace bb {
 
@@ -28,8 +34,10 @@ int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, int32_t* 
 namespace {
 
 constexpr int DK_THREADS = 128;  // 4 warps
-constexpr int DK_BN = 64;        // keys per block
-constexpr int DK_MAXROWS = 16;   // query heads per route group
+constexpr int DK_WARPS = 4;
+constexpr int DK_BN = 64;        // keys per stage: 16 per warp
+constexpr int DK_NST = 3;        // stages in the ring (two in flight while one is used); 2 CTAs a SM
+constexpr int DK_MAXROWS = 16;   // query heads per route group: one m16 tile
 constexpr float LOG2E_F_DK = 1.4426950408889634f;
 
 struct DecodeParams {
@@ -50,9 +58,19 @@ struct DecodeParams {
   float* probs;     // [kv_heads][cap]
 };
 
+// Shared-memory plan of one CTA: a ring of DK_NST stages of 64 K rows (and 64 V rows), padded to
+// DP + 8 elements so that ldmatrix reads are free of bank conflicts; 16 query rows; 64 positions a
+// stage. After the key loop the ring is reused for the cross-warp merge (m, l and O per warp).
 template <int DP> struct DkSmem {
-  static constexpr int LD = DP + 8;  // padded row (elements): conflict-free 16-byte reads
-  static constexpr size_t kv_bytes = (size_t)DK_BN * LD * 2;  // one 64-key block of K or V
+  static constexpr int LD = DP + 8;
+  static constexpr size_t tile = (size_t)DK_BN * LD * 2;                  // one stage of K (or V)
+  static constexpr size_t q_bytes = (size_t)DK_MAXROWS * LD * 2;
+  static constexpr size_t pos_bytes = (size_t)DK_NST * DK_BN * 4 + DK_NST * 8 + 16;  // + full barriers, abort flag
+  static constexpr size_t merge_bytes = (size_t)DK_WARPS * DK_MAXROWS * (DP + 2) * 4;
+  static constexpr size_t ring(bool with_v) {
+    return DK_NST * tile * (with_v ? 2 : 1) > merge_bytes ? DK_NST * tile * (with_v ? 2 : 1) : merge_bytes;
+  }
+  static constexpr size_t bytes(bool with_v) { return ring(with_v) + q_bytes + pos_bytes; }
 };
 
 __device__ __forceinline__ int64_t cache_len(const DecodeParams& p) {
@@ -70,301 +88,478 @@ __device__ __forceinline__ int64_t virtual_pos(const DecodeParams& p, int64_t r,
   return (pos >= 0 && pos < n) ? pos : -1;
 }
 
-// 64 rows of a K or V block (rows at positions pos_s[i]; -1 -> zero row) into padded shared memory.
-template <typename T, int DP>
-__device__ __forceinline__ void load_block(const T* base, int64_t s_t, const int64_t* pos_s, T* dst, int64_t d) {
-  constexpr int LD = DkSmem<DP>::LD;
-  constexpr int CH = DP / 8;
-  for (int c = threadIdx.x; c < DK_BN * CH; c += DK_THREADS) {
-    const int i = c / CH, ch = c % CH;
-    const int64_t pos = pos_s[i];
-    const bool ok = pos >= 0 && ch * 8 < d;
-    const T* src = ok ? base + pos * s_t + ch * 8 : base;
-    cp_async_16(smem_u32(dst + i * LD + ch * 8), src, ok);
+// Row gather: thread t copies row t % 64 of the stage's K (t < 64) or V (t >= 64) with one bulk
+// copy (d * 2 bytes) that completes on the stage's full barrier; a row that is not a key is
+// zero-filled instead. Every thread arrives on the barrier once a stage (count DK_THREADS).
+__device__ __forceinline__ void bulk_row(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+template <typename T>
+__device__ __forceinline__ void stage_row(T* row, const T* src, bool valid, int64_t d, uint32_t bar) {
+  if (valid) {
+    tc::mbar_expect_tx(bar, (uint32_t)(d * 2));
+    bulk_row(smem_u32(row), src, (uint32_t)(d * 2), bar);
+  } else {
+    for (int64_t c = 0; c < d; c += 8) *reinterpret_cast<uint4*>(row + c) = make_uint4(0u, 0u, 0u, 0u);
+    // This thread's later bulk copies into the row (async proxy) must land after these stores.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc::mbar_arrive(bar);
   }
 }
 
-// Scores of this lane's two keys (lane, lane + 32) of the block for one query row (fp32 q in smem).
+// The query rows of a route group into shared memory (zero past `rows` and past d), as bf16/f16.
 template <typename T, int DP>
-__device__ __forceinline__ void row_scores(const float* qrow, const T* ks, int lane, float& s0, float& s1) {
+__device__ __forceinline__ void load_q(const DecodeParams& p, int64_t first_head, int rows, T* qs) {
   constexpr int LD = DkSmem<DP>::LD;
-  float a0 = 0.f, a1 = 0.f;
-  const T* k0 = ks + lane * LD;
-  const T* k1 = ks + (lane + 32) * LD;
-#pragma unroll 4
-  for (int c = 0; c < DP; c += 8) {
-    const uint4 u0 = *reinterpret_cast<const uint4*>(k0 + c);
-    const uint4 u1 = *reinterpret_cast<const uint4*>(k1 + c);
-    const T* e0 = reinterpret_cast<const T*>(&u0);
-    const T* e1 = reinterpret_cast<const T*>(&u1);
+  const T* Q = static_cast<const T*>(p.q);
+  for (int i = threadIdx.x; i < DK_MAXROWS * DP; i += DK_THREADS) {
+    const int row = i / DP, c = i % DP;
+    qs[row * LD + c] = (row < rows && c < p.d) ? Q[(first_head + row) * p.sq_h + c] : Elem<T>::from_f(0.f);
+  }
+}
+
+// A fragments of the 16 x DP query tile (m16n8k16 row-major A).
+template <typename T, int DP>
+__device__ __forceinline__ void q_frags(const T* qs, uint32_t (&qf)[DP / 16][4]) {
+  constexpr int LD = DkSmem<DP>::LD;
+  const int lane = threadIdx.x % 32;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float qv = qrow[c + e];
-      a0 = fmaf(qv, Elem<T>::to_f(e0[e]), a0);
-      a1 = fmaf(qv, Elem<T>::to_f(e1[e]), a1);
-    }
-  }
-  s0 = a0;
-  s1 = a1;
+  for (int kk = 0; kk < DP / 16; ++kk)
+    ldmatrix_x4(qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], smem_u32(qs + (lane % 16) * LD + kk * 16 + (lane / 16) * 8));
 }
 
+// S (16 rows x this warp's 16 keys) = Q K^T: two n8 tiles.
 template <typename T, int DP>
-__global__ void __launch_bounds__(DK_THREADS) decode_partial_kernel(DecodeParams p) {
+__device__ __forceinline__ void warp_scores(const uint32_t (&qf)[DP / 16][4], const T* kb, int key0, float (&s)[2][4]) {
   constexpr int LD = DkSmem<DP>::LD;
+  const int lane = threadIdx.x % 32;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) s[t][0] = s[t][1] = s[t][2] = s[t][3] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < DP / 16; ++kk) {
+    uint32_t b0, b1, b2, b3;
+    ldmatrix_x4(b0, b1, b2, b3, smem_u32(kb + (key0 + (lane / 16) * 8 + (lane % 8)) * LD + kk * 16 + ((lane / 8) % 2) * 8));
+    const uint32_t bA[2] = {b0, b1}, bB[2] = {b2, b3};
+    mma_16816<T>(s[0], qf[kk], bA);
+    mma_16816<T>(s[1], qf[kk], bB);
+  }
+}
+
+// Split-K sparse decoding, one CTA per (route row, split). Each warp runs its own online softmax
+// over 16 keys of every 64-key stage (S and P.V on mma.sync m16n8k16, rows = the group's query
+// heads); the four warps' states are merged once at the end.
+template <typename T, int DP>
+__global__ void __launch_bounds__(DK_THREADS, 2) decode_partial_kernel(DecodeParams p) {
+  using S = DkSmem<DP>;
+  constexpr int LD = S::LD;
   extern __shared__ __align__(128) unsigned char smem[];
-  T* ks = reinterpret_cast<T*>(smem);                                   // [2][64][LD]
-  T* vs = ks + 2 * DK_BN * LD;                                          // [2][64][LD]
-  float* qs = reinterpret_cast<float*>(vs + 2 * DK_BN * LD);            // [rows][DP]
-  float* ps = qs + DK_MAXROWS * DP;                                     // [rows][64] P (dtype-rounded)
-  int64_t* pos_s = reinterpret_cast<int64_t*>(ps + DK_MAXROWS * DK_BN);  // [2][64]
+  T* ks = reinterpret_cast<T*>(smem);                        // [NST][64][LD]
+  T* vs = ks + DK_NST * DK_BN * LD;                          // [NST][64][LD]
+  constexpr size_t ring = S::ring(true);
+  T* qs = reinterpret_cast<T*>(smem + ring);                 // [16][LD]
+  int32_t* pos_s = reinterpret_cast<int32_t*>(smem + ring + S::q_bytes);  // [NST][64]
+  uint64_t* full = reinterpret_cast<uint64_t*>(pos_s + DK_NST * DK_BN);   // [NST]
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(full + DK_NST);
   const int64_t r = blockIdx.x, split = blockIdx.y;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int64_t n = cache_len(p);
-  const int64_t kv = (r * p.rows) / p.groups;
   const int rows = (int)p.rows;
+  const int64_t kv = (r * p.rows) / p.groups;
   const T* K = static_cast<const T*>(p.k) + kv * p.sk_h;
   const T* V = static_cast<const T*>(p.v) + kv * p.sv_h;
-  // query rows (fp32, pre-scaled to log2 units as scores * scale * log2 e)
-  const T* Q = static_cast<const T*>(p.q);
-  for (int i = threadIdx.x; i < rows * DP; i += DK_THREADS) {
-    const int row = i / DP, c = i % DP;
-    qs[i] = c < p.d ? Elem<T>::to_f(Q[(r * p.rows + row) * p.sq_h + c]) : 0.f;
-  }
   const int64_t total = p.front + p.window + p.route_k;
   const int64_t j0 = split * p.split_len;
   const int64_t j1 = min(j0 + p.split_len, total);
   const int nblocks = j0 < j1 ? (int)cdiv(j1 - j0, (int64_t)DK_BN) : 0;
-  // per-warp state for its rows (warp w owns rows w, w + 4, ...), lane owns dims 4*lane .. 4*lane+3
-  constexpr int RPW = DK_MAXROWS / 4;
-  constexpr int DPL = DP / 32;  // dims per lane
-  float m[RPW], l[RPW], acc[RPW][DPL];
-#pragma unroll
-  for (int i = 0; i < RPW; ++i) {
-    m[i] = -1.0e20f;
-    l[i] = 0.f;
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) acc[i][e] = 0.f;
+  if (p.d < DP)  // columns past d are never copied: keep them zero
+    for (int i = threadIdx.x; i < (int)(2 * DK_NST * S::tile / 16); i += DK_THREADS)
+      reinterpret_cast<uint4*>(smem)[i] = make_uint4(0u, 0u, 0u, 0u);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // before any bulk copy into the ring
+  load_q<T, DP>(p, r * p.rows, rows, qs);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < DK_NST; ++i) tc::mbar_init(smem_u32(full + i), DK_THREADS);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  auto positions = [&](int b, int buf) {
-    for (int i = threadIdx.x; i < DK_BN; i += DK_THREADS) {
-      const int64_t j = j0 + (int64_t)b * DK_BN + i;
-      pos_s[buf * DK_BN + i] = j < j1 ? virtual_pos(p, r, j, n) : -1;
-    }
+  __syncthreads();
+
+  // Thread t moves row t % 64 of K (t < 64) or V (t >= 64); `pf` holds the position of its row in
+  // the next stage to issue (looked up one stage early, so a route's index load is off the path).
+  const int lrow = threadIdx.x % DK_BN;
+  const bool is_k = threadIdx.x < DK_BN;
+  const T* src_base = is_k ? K : V;
+  const int64_t src_t = is_k ? p.sk_t : p.sv_t;
+  T* dst_ring = is_k ? ks : vs;
+  auto fetch = [&](int blk) -> int32_t {
+    const int64_t j = j0 + (int64_t)blk * DK_BN + lrow;
+    return (blk < nblocks && j < j1) ? (int32_t)virtual_pos(p, r, j, n) : -1;
   };
-  if (nblocks > 0) {
-    positions(0, 0);
-    __syncthreads();
-    load_block<T, DP>(K, p.sk_t, pos_s, ks, p.d);
-    load_block<T, DP>(V, p.sv_t, pos_s, vs, p.d);
-    cp_async_commit();
-  }
-  for (int b = 0; b < nblocks; ++b) {
-    const int buf = b & 1;
-    if (b + 1 < nblocks) {
-      positions(b + 1, buf ^ 1);
-      __syncthreads();
-      load_block<T, DP>(K, p.sk_t, pos_s + (buf ^ 1) * DK_BN, ks + (buf ^ 1) * DK_BN * LD, p.d);
-      load_block<T, DP>(V, p.sv_t, pos_s + (buf ^ 1) * DK_BN, vs + (buf ^ 1) * DK_BN * LD, p.d);
+  auto issue = [&](int blk, int32_t pos) {
+    if (blk >= nblocks) return;
+    const int slot = blk % DK_NST;
+    if (is_k) pos_s[slot * DK_BN + lrow] = pos;
+    stage_row<T>(dst_ring + (slot * DK_BN + lrow) * LD, src_base + (int64_t)(pos < 0 ? 0 : pos) * src_t, pos >= 0,
+                 p.d, smem_u32(full + slot));
+  };
+#pragma unroll 1
+  for (int s = 0; s < DK_NST - 1; ++s) issue(s, fetch(s));
+  int32_t pf = fetch(DK_NST - 1);
+  uint32_t qf[DP / 16][4];
+  q_frags<T, DP>(qs, qf);
+
+  float o[DP / 8][4];
+#pragma unroll
+  for (int i = 0; i < DP / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -1.0e20f, m1 = -1.0e20f, l0 = 0.f, l1 = 0.f;
+  const int key0 = warp * 16;
+  const bool two = rows > 8;  // query rows 8..15 in use (c2/c3 of the fragments)
+  int b = 0;
+#pragma unroll 1
+  for (; b < nblocks; ++b) {
+    const int slot = b % DK_NST;
+    const bool ok = tc::mbar_wait(smem_u32(full + slot), (uint32_t)((b / DK_NST) & 1), abort_flag, 40);
+    if (!__syncthreads_and(ok)) break;  // stage b landed for all; stage b - 1 is free
+    issue(b + DK_NST - 1, pf);
+    pf = fetch(b + DK_NST);
+    const T* kb = ks + slot * DK_BN * LD;
+    const T* vb = vs + slot * DK_BN * LD;
+    const int32_t* ps = pos_s + slot * DK_BN;
+    float s[2][4];
+    warp_scores<T, DP>(qf, kb, key0, s);
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int kk = key0 + t * 8 + 2 * (lane % 4);
+      const bool v0 = ps[kk] >= 0, v1 = ps[kk + 1] >= 0;
+      s[t][0] = v0 ? s[t][0] * p.scale_log2 : -INFINITY;
+      s[t][1] = v1 ? s[t][1] * p.scale_log2 : -INFINITY;
+      s[t][2] = v0 ? s[t][2] * p.scale_log2 : -INFINITY;
+      s[t][3] = v1 ? s[t][3] * p.scale_log2 : -INFINITY;
+      mx0 = fmaxf(mx0, fmaxf(s[t][0], s[t][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[t][2], s[t][3]));
     }
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    const T* kb = ks + buf * DK_BN * LD;
-    const T* vb = vs + buf * DK_BN * LD;
-    const bool ok0 = pos_s[buf * DK_BN + lane] >= 0, ok1 = pos_s[buf * DK_BN + lane + 32] >= 0;
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    const float n0 = fmaxf(m0, mx0);  // m starts at the -1e20 floor
+    const float a0 = fast_exp2(m0 - n0);
+    m0 = n0;
+    float pr[2][4];
 #pragma unroll
-    for (int i = 0; i < RPW; ++i) {
-      const int row = warp + 4 * i;
-      if (row >= rows) break;
-      float s0, s1;
-      row_scores<T, DP>(qs + row * DP, kb, lane, s0, s1);
-      s0 = ok0 ? s0 * p.scale_log2 : -INFINITY;
-      s1 = ok1 ? s1 * p.scale_log2 : -INFINITY;
-      float mx = fmaxf(s0, s1);
+    for (int t = 0; t < 2; ++t) {
+      pr[t][0] = fast_exp2(s[t][0] - n0);
+      pr[t][1] = fast_exp2(s[t][1] - n0);
+      pr[t][2] = pr[t][3] = 0.f;
+    }
+    float a1 = 1.f;
+    if (two) {
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float n1 = fmaxf(m1, mx1);
+      a1 = fast_exp2(m1 - n1);
+      m1 = n1;
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      const float mnew = fmaxf(fmaxf(m[i], mx), -1.0e20f);
-      const float alpha = fast_exp2(m[i] - mnew);
-      // P rounded to the cache dtype before P.V (kernels/bigger_bird_decode.py:58); the sum uses
-      // the unrounded values (:59).
-      const float p0 = fast_exp2(s0 - mnew), p1 = fast_exp2(s1 - mnew);
-      float sum = p0 + p1;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-      ps[row * DK_BN + lane] = Elem<T>::round(p0);
-      ps[row * DK_BN + lane + 32] = Elem<T>::round(p1);
-      __syncwarp();
-      float a[DPL];
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) a[e] = 0.f;
-      for (int key = 0; key < DK_BN; ++key) {
-        const float pk = ps[row * DK_BN + key];
-        const T* vr = vb + key * LD + lane * DPL;
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) a[e] = fmaf(pk, Elem<T>::to_f(vr[e]), a[e]);
+      for (int t = 0; t < 2; ++t) {
+        pr[t][2] = fast_exp2(s[t][2] - n1);
+        pr[t][3] = fast_exp2(s[t][3] - n1);
       }
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) acc[i][e] = acc[i][e] * alpha + a[e];
-      l[i] = l[i] * alpha + sum;
-      m[i] = mnew;
-      __syncwarp();
+      l1 = l1 * a1 + (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
     }
-    __syncthreads();
+    // l from the unrounded probabilities (kernels/bigger_bird_decode.py:59); P.V with P rounded
+    // to the cache dtype (:58), which the A fragment packing does.
+    l0 = l0 * a0 + (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
+    const uint32_t a[4] = {pack2<T>(pr[0][0], pr[0][1]), pack2<T>(pr[0][2], pr[0][3]),
+                           pack2<T>(pr[1][0], pr[1][1]), pack2<T>(pr[1][2], pr[1][3])};
+    if (!__all_sync(0xffffffffu, a0 == 1.f && a1 == 1.f)) {  // running max moved: rescale O
+#pragma unroll
+      for (int i = 0; i < DP / 8; ++i) {
+        o[i][0] *= a0;
+        o[i][1] *= a0;
+        o[i][2] *= a1;
+        o[i][3] *= a1;
+      }
+    }
+#pragma unroll
+    for (int dp = 0; dp < DP / 16; ++dp) {
+      uint32_t b0, b1, b2, b3;
+      ldmatrix_x4_trans(b0, b1, b2, b3,
+                        smem_u32(vb + (key0 + ((lane / 8) % 2) * 8 + (lane % 8)) * LD + dp * 16 + (lane / 16) * 8));
+      const uint32_t bA[2] = {b0, b1}, bB[2] = {b2, b3};
+      mma_16816<T>(o[dp * 2], a, bA);
+      mma_16816<T>(o[dp * 2 + 1], a, bB);
+    }
   }
-  // partials: (m, l, acc) per row of this chunk
+  if (b < nblocks) {
+    // A wait gave up (fault recorded): let the copies still in flight land, then leave.
+    for (int blk = b; blk < min(nblocks, b + DK_NST - 1); ++blk)
+      tc::mbar_drain(smem_u32(full + blk % DK_NST), (uint32_t)((blk / DK_NST) & 1));
+    return;
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  // Merge the four warps: [warp][row] m and l, then [warp][row][DP] O, in the ring's space.
+  __syncthreads();
+  float* wm = reinterpret_cast<float*>(smem);
+  float* wl = wm + DK_WARPS * DK_MAXROWS;
+  float* wo = wl + DK_WARPS * DK_MAXROWS;
+  const int g = lane / 4, c = 2 * (lane % 4);
+  if (lane % 4 == 0) {
+    wm[warp * DK_MAXROWS + g] = m0;
+    wl[warp * DK_MAXROWS + g] = l0;
+    wm[warp * DK_MAXROWS + g + 8] = m1;
+    wl[warp * DK_MAXROWS + g + 8] = l1;
+  }
 #pragma unroll
-  for (int i = 0; i < RPW; ++i) {
-    const int row = warp + 4 * i;
-    if (row >= rows) break;
-    const int64_t at = (r * p.splits + split) * p.rows + row;
-    if (lane == 0) {
-      p.part_m[at] = m[i];
-      p.part_l[at] = l[i];
+  for (int i = 0; i < DP / 8; ++i) {
+    *reinterpret_cast<float2*>(wo + (warp * DK_MAXROWS + g) * DP + i * 8 + c) = make_float2(o[i][0], o[i][1]);
+    *reinterpret_cast<float2*>(wo + (warp * DK_MAXROWS + g + 8) * DP + i * 8 + c) = make_float2(o[i][2], o[i][3]);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < rows * DP; i += DK_THREADS) {
+    const int row = i / DP, col = i % DP;
+    float M = -1.0e20f;
+#pragma unroll
+    for (int w = 0; w < DK_WARPS; ++w) M = fmaxf(M, wm[w * DK_MAXROWS + row]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < DK_WARPS; ++w) {
+      const float f = fast_exp2(wm[w * DK_MAXROWS + row] - M);
+      L += wl[w * DK_MAXROWS + row] * f;
+      A += wo[(w * DK_MAXROWS + row) * DP + col] * f;
     }
-#pragma unroll
-    for (int e = 0; e < DPL; ++e)
-      if (lane * DPL + e < p.d) p.part_acc[at * p.d + lane * DPL + e] = acc[i][e];
+    const int64_t at = (r * p.splits + split) * p.rows + row;
+    if (col == 0) {
+      p.part_m[at] = M;
+      p.part_l[at] = L;
+    }
+    if (col < p.d) p.part_acc[at * p.d + col] = A;
   }
 }
 
-// One warp per query head: merges its splits.
+// One CTA per query head merges its splits: w_s = exp2(m_s - max m), out = sum w_s acc_s / sum w_s l_s.
 template <typename T>
 __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeParams p) {
-  const int64_t h = (int64_t)blockIdx.x * 4 + threadIdx.x / 32;
-  const int lane = threadIdx.x % 32;
-  if (h >= p.heads) return;
+  extern __shared__ float wsm[];  // [splits]
+  __shared__ float red[4];
+  const int64_t h = blockIdx.x;
   const int64_t r = h / p.rows, row = h % p.rows;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int S = (int)p.splits;
+  auto at = [&](int s) { return (r * p.splits + s) * p.rows + row; };
   float M = -INFINITY;
-  for (int64_t s = 0; s < p.splits; ++s) M = fmaxf(M, p.part_m[(r * p.splits + s) * p.rows + row]);
-  float L = 0.f;
-  for (int64_t s = 0; s < p.splits; ++s) {
-    const int64_t at = (r * p.splits + s) * p.rows + row;
-    L += p.part_l[at] * fast_exp2(p.part_m[at] - M);
+  for (int s = threadIdx.x; s < S; s += 128) {
+    const float m = p.part_m[at(s)];
+    wsm[s] = m;
+    M = fmaxf(M, m);
   }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  if (lane == 0) red[warp] = M;
+  __syncthreads();
+  M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  float L = 0.f;
+  for (int s = threadIdx.x; s < S; s += 128) {
+    const float w = fast_exp2(wsm[s] - M);
+    wsm[s] = w;
+    L += p.part_l[at(s)] * w;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+  __syncthreads();
+  if (lane == 0) red[warp] = L;
+  __syncthreads();
+  L = (red[0] + red[1]) + (red[2] + red[3]);
   T* o = static_cast<T*>(p.out) + h * p.so_h;
-  for (int64_t c = lane; c < p.d; c += 32) {
-    float a = 0.f;
-    for (int64_t s = 0; s < p.splits; ++s) {
-      const int64_t at = (r * p.splits + s) * p.rows + row;
-      a += p.part_acc[at * p.d + c] * fast_exp2(p.part_m[at] - M);
+  for (int64_t col = threadIdx.x; col < p.d; col += 128) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    int s = 0;
+    for (; s + 4 <= S; s += 4) {
+      a0 += p.part_acc[at(s) * p.d + col] * wsm[s];
+      a1 += p.part_acc[at(s + 1) * p.d + col] * wsm[s + 1];
+      a2 += p.part_acc[at(s + 2) * p.d + col] * wsm[s + 2];
+      a3 += p.part_acc[at(s + 3) * p.d + col] * wsm[s + 3];
     }
-    o[c] = Elem<T>::from_f(a / L);
+    for (; s < S; ++s) a0 += p.part_acc[at(s) * p.d + col] * wsm[s];
+    o[col] = Elem<T>::from_f(((a0 + a1) + (a2 + a3)) / L);
   }
 }
 
-// Decode routing pass 1: grid (kv_heads, splits); chunk of contiguous cached keys.
+// Decode routing pass 1: one CTA per (KV head, chunk of contiguous cached keys). Scores of the
+// group's query heads on mma.sync, stored log2-scaled, plus the chunk's softmax statistics.
 template <typename T, int DP>
 __global__ void __launch_bounds__(DK_THREADS) droute_scores_kernel(DecodeParams p) {
-  constexpr int LD = DkSmem<DP>::LD;
+  using S = DkSmem<DP>;
+  constexpr int LD = S::LD;
   extern __shared__ __align__(128) unsigned char smem[];
-  T* ks = reinterpret_cast<T*>(smem);                         // [2][64][LD]
-  float* qs = reinterpret_cast<float*>(ks + 2 * DK_BN * LD);  // [rows][DP]
-  int64_t* pos_s = reinterpret_cast<int64_t*>(qs + DK_MAXROWS * DP);
+  T* ks = reinterpret_cast<T*>(smem);  // [NST][64][LD]
+  constexpr size_t ring = S::ring(false);
+  T* qs = reinterpret_cast<T*>(smem + ring);
+  int32_t* pos_s = reinterpret_cast<int32_t*>(smem + ring + S::q_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(pos_s + DK_NST * DK_BN);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(full + DK_NST);
   const int64_t kv = blockIdx.x, split = blockIdx.y;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int64_t n = cache_len(p);
   const int rows = (int)p.groups;
   const T* K = static_cast<const T*>(p.k) + kv * p.sk_h;
-  const T* Q = static_cast<const T*>(p.q);
-  for (int i = threadIdx.x; i < rows * DP; i += DK_THREADS) {
-    const int row = i / DP, c = i % DP;
-    qs[i] = c < p.d ? Elem<T>::to_f(Q[(kv * p.groups + row) * p.sq_h + c]) : 0.f;
-  }
   const int64_t j0 = split * p.split_len;
   const int64_t j1 = min(j0 + p.split_len, n);
   const int nblocks = j0 < j1 ? (int)cdiv(j1 - j0, (int64_t)DK_BN) : 0;
-  constexpr int RPW = DK_MAXROWS / 4;
-  float m[RPW], l[RPW];
-#pragma unroll
-  for (int i = 0; i < RPW; ++i) {
-    m[i] = -1.0e20f;
-    l[i] = 0.f;
+  if (p.d < DP)
+    for (int i = threadIdx.x; i < (int)(DK_NST * S::tile / 16); i += DK_THREADS)
+      reinterpret_cast<uint4*>(smem)[i] = make_uint4(0u, 0u, 0u, 0u);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // before any bulk copy into the ring
+  load_q<T, DP>(p, kv * p.groups, rows, qs);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < DK_NST; ++i) tc::mbar_init(smem_u32(full + i), DK_THREADS);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  auto positions = [&](int b, int buf) {
-    for (int i = threadIdx.x; i < DK_BN; i += DK_THREADS) {
-      const int64_t j = j0 + (int64_t)b * DK_BN + i;
-      pos_s[buf * DK_BN + i] = j < j1 ? j : -1;
+  __syncthreads();
+  const int lrow = threadIdx.x % DK_BN;
+  const bool loader = threadIdx.x < DK_BN;
+  auto issue = [&](int blk) {
+    if (blk >= nblocks) return;
+    const int slot = blk % DK_NST;
+    if (!loader) {
+      tc::mbar_arrive(smem_u32(full + slot));
+      return;
     }
+    const int64_t j = j0 + (int64_t)blk * DK_BN + lrow;
+    const int32_t pos = j < j1 ? (int32_t)j : -1;
+    pos_s[slot * DK_BN + lrow] = pos;
+    stage_row<T>(ks + (slot * DK_BN + lrow) * LD, K + (int64_t)(pos < 0 ? 0 : pos) * p.sk_t, pos >= 0, p.d,
+                 smem_u32(full + slot));
   };
-  if (nblocks > 0) {
-    positions(0, 0);
-    __syncthreads();
-    load_block<T, DP>(K, p.sk_t, pos_s, ks, p.d);
-    cp_async_commit();
+#pragma unroll 1
+  for (int s = 0; s < DK_NST - 1; ++s) issue(s);
+  uint32_t qf[DP / 16][4];
+  q_frags<T, DP>(qs, qf);
+  float m0 = -1.0e20f, m1 = -1.0e20f, l0 = 0.f, l1 = 0.f;
+  const int key0 = warp * 16;
+  const int g = lane / 4, c = 2 * (lane % 4);
+  const bool two = rows > 8;
+  float* srow0 = p.scores + (kv * p.groups + g) * p.cap;
+  float* srow1 = p.scores + (kv * p.groups + (two ? g + 8 : g)) * p.cap;
+  int b = 0;
+#pragma unroll 1
+  for (; b < nblocks; ++b) {
+    const int slot = b % DK_NST;
+    const bool ok = tc::mbar_wait(smem_u32(full + slot), (uint32_t)((b / DK_NST) & 1), abort_flag, 41);
+    if (!__syncthreads_and(ok)) break;
+    issue(b + DK_NST - 1);
+    const int32_t* ps = pos_s + slot * DK_BN;
+    float s[2][4];
+    warp_scores<T, DP>(qf, ks + slot * DK_BN * LD, key0, s);
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int kk = key0 + t * 8 + c;
+      const int32_t q0 = ps[kk], q1 = ps[kk + 1];
+      s[t][0] = q0 >= 0 ? s[t][0] * p.scale_log2 : -INFINITY;
+      s[t][1] = q1 >= 0 ? s[t][1] * p.scale_log2 : -INFINITY;
+      s[t][2] = q0 >= 0 ? s[t][2] * p.scale_log2 : -INFINITY;
+      s[t][3] = q1 >= 0 ? s[t][3] * p.scale_log2 : -INFINITY;
+      if (g < rows) {
+        if (q0 >= 0) srow0[q0] = s[t][0];
+        if (q1 >= 0) srow0[q1] = s[t][1];
+      }
+      if (two && g + 8 < rows) {
+        if (q0 >= 0) srow1[q0] = s[t][2];
+        if (q1 >= 0) srow1[q1] = s[t][3];
+      }
+      mx0 = fmaxf(mx0, fmaxf(s[t][0], s[t][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[t][2], s[t][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    const float n0 = fmaxf(m0, mx0);
+    l0 = l0 * fast_exp2(m0 - n0) + (fast_exp2(s[0][0] - n0) + fast_exp2(s[0][1] - n0)) +
+         (fast_exp2(s[1][0] - n0) + fast_exp2(s[1][1] - n0));
+    m0 = n0;
+    if (two) {
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float n1 = fmaxf(m1, mx1);
+      l1 = l1 * fast_exp2(m1 - n1) + (fast_exp2(s[0][2] - n1) + fast_exp2(s[0][3] - n1)) +
+           (fast_exp2(s[1][2] - n1) + fast_exp2(s[1][3] - n1));
+      m1 = n1;
+    }
   }
-  for (int b = 0; b < nblocks; ++b) {
-    const int buf = b & 1;
-    if (b + 1 < nblocks) {
-      positions(b + 1, buf ^ 1);
-      __syncthreads();
-      load_block<T, DP>(K, p.sk_t, pos_s + (buf ^ 1) * DK_BN, ks + (buf ^ 1) * DK_BN * LD, p.d);
-    }
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    const T* kb = ks + buf * DK_BN * LD;
-    const int64_t pos0 = pos_s[buf * DK_BN + lane], pos1 = pos_s[buf * DK_BN + lane + 32];
-#pragma unroll
-    for (int i = 0; i < RPW; ++i) {
-      const int row = warp + 4 * i;
-      if (row >= rows) break;
-      float s0, s1;
-      row_scores<T, DP>(qs + row * DP, kb, lane, s0, s1);
-      s0 = pos0 >= 0 ? s0 * p.scale_log2 : -INFINITY;
-      s1 = pos1 >= 0 ? s1 * p.scale_log2 : -INFINITY;
-      float* srow = p.scores + (kv * p.groups + row) * p.cap;
-      if (pos0 >= 0) srow[pos0] = s0;
-      if (pos1 >= 0) srow[pos1] = s1;
-      float mx = fmaxf(s0, s1);
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      const float mnew = fmaxf(fmaxf(m[i], mx), -1.0e20f);
-      float sum = fast_exp2(s0 - mnew) + fast_exp2(s1 - mnew);
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-      l[i] = l[i] * fast_exp2(m[i] - mnew) + sum;
-      m[i] = mnew;
-    }
-    __syncthreads();
+  if (b < nblocks) {
+    for (int blk = b; blk < min(nblocks, b + DK_NST - 1); ++blk)
+      tc::mbar_drain(smem_u32(full + blk % DK_NST), (uint32_t)((blk / DK_NST) & 1));
+    return;
   }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  __syncthreads();
+  float* wm = reinterpret_cast<float*>(smem);
+  float* wl = wm + DK_WARPS * DK_MAXROWS;
+  if (lane % 4 == 0) {
+    wm[warp * DK_MAXROWS + g] = m0;
+    wl[warp * DK_MAXROWS + g] = l0;
+    wm[warp * DK_MAXROWS + g + 8] = m1;
+    wl[warp * DK_MAXROWS + g + 8] = l1;
+  }
+  __syncthreads();
+  if (threadIdx.x < rows) {
+    const int row = threadIdx.x;
+    float M = -1.0e20f;
 #pragma unroll
-  for (int i = 0; i < RPW; ++i) {
-    const int row = warp + 4 * i;
-    if (row >= rows) break;
-    if (lane == 0) {
-      const int64_t at = (kv * p.splits + split) * p.groups + row;
-      p.part_m[at] = m[i];
-      p.part_l[at] = l[i];
-    }
+    for (int w = 0; w < DK_WARPS; ++w) M = fmaxf(M, wm[w * DK_MAXROWS + row]);
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < DK_WARPS; ++w) L += wl[w * DK_MAXROWS + row] * fast_exp2(wm[w * DK_MAXROWS + row] - M);
+    const int64_t at = (kv * p.splits + split) * p.groups + row;
+    p.part_m[at] = M;
+    p.part_l[at] = L;
   }
 }
 
-// Decode routing pass 2: grid (kv_heads, cdiv(cap, 256)); one thread per cached position.
+// Decode routing pass 2: grid (kv_heads, cdiv(cap, 1024)); four positions a thread. The group's
+// merged statistics come first, 16 threads a query head.
 __global__ void __launch_bounds__(256) droute_pool_kernel(DecodeParams p) {
   const int64_t kv = blockIdx.x;
-  const int64_t pos = (int64_t)blockIdx.y * 256 + threadIdx.x;
   const int64_t n = cache_len(p);
   __shared__ float sm[DK_MAXROWS], sinv[DK_MAXROWS];
-  if (threadIdx.x < p.groups) {
-    const int row = threadIdx.x;
+  {
+    const int row = threadIdx.x / 16, sub = threadIdx.x % 16;
+    const bool live = row < p.groups;
     float M = -1.0e20f;
-    for (int64_t s = 0; s < p.splits; ++s) M = fmaxf(M, p.part_m[(kv * p.splits + s) * p.groups + row]);
+    if (live)
+      for (int64_t s = sub; s < p.splits; s += 16) M = fmaxf(M, p.part_m[(kv * p.splits + s) * p.groups + row]);
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
     float L = 0.f;
-    for (int64_t s = 0; s < p.splits; ++s) {
-      const int64_t at = (kv * p.splits + s) * p.groups + row;
-      L += p.part_l[at] * fast_exp2(p.part_m[at] - M);
+    if (live)
+      for (int64_t s = sub; s < p.splits; s += 16) {
+        const int64_t at = (kv * p.splits + s) * p.groups + row;
+        L += p.part_l[at] * fast_exp2(p.part_m[at] - M);
+      }
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    if (live && sub == 0) {
+      sm[row] = M;
+      sinv[row] = 1.f / fmaxf(L, 1.0e-30f);
     }
-    sm[row] = M;
-    sinv[row] = 1.f / fmaxf(L, 1.0e-30f);
   }
   __syncthreads();
-  if (pos >= p.cap) return;
-  float acc = 0.f;
-  if (pos < n)
-    for (int64_t row = 0; row < p.groups; ++row)
-      acc += fast_exp2(p.scores[(kv * p.groups + row) * p.cap + pos] - sm[row]) * sinv[row];
-  const bool keep = pos >= p.front && pos < n - p.window;
-  p.probs[kv * p.cap + pos] = keep ? acc / (float)p.groups : -1.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t pos = (int64_t)blockIdx.y * 1024 + i * 256 + threadIdx.x;
+    if (pos >= p.cap) break;
+    float acc = 0.f;
+    if (pos < n)
+      for (int64_t row = 0; row < p.groups; ++row)
+        acc += fast_exp2(p.scores[(kv * p.groups + row) * p.cap + pos] - sm[row]) * sinv[row];
+    const bool keep = pos >= p.front && pos < n - p.window;
+    p.probs[kv * p.cap + pos] = keep ? acc / (float)p.groups : -1.f;
+  }
 }
 
 struct DecodePlan {
@@ -374,6 +569,18 @@ struct DecodePlan {
 
 int dpad(int64_t d) { return d <= 32 ? 32 : (d <= 64 ? 64 : 128); }
 
+size_t dk_smem(int dp, bool with_v) {
+  return dp == 32 ? DkSmem<32>::bytes(with_v) : (dp == 64 ? DkSmem<64>::bytes(with_v) : DkSmem<128>::bytes(with_v));
+}
+
+// Splits that fill the GPU in one wave: resident CTAs a SM (from shared memory) x SMs, over the
+// CTAs a split count multiplies (route rows); at least two stages of keys a split, at most 8192.
+int64_t auto_splits(int64_t keys, int64_t ctas_per_split, size_t smem) {
+  const int64_t per_sm = std::max<int64_t>(1, std::min<int64_t>(8, (int64_t)(233472 / (smem + 1024))));
+  const int64_t wave = std::max<int64_t>(1, per_sm * num_sms() / ctas_per_split);
+  return std::max<int64_t>(1, std::min<int64_t>({cdiv(keys, (int64_t)2 * DK_BN), wave, (int64_t)8192}));
+}
+
 int check_common(const bb_decode_args* a, int64_t rows_per_group_max) {
   if (!a) return fail(BB_ERR_ARG, "decode: null args");
   if (a->dtype != BB_F16 && a->dtype != BB_BF16) return fail(BB_ERR_DTYPE, "decode requires fp16 or bf16");
@@ -381,6 +588,7 @@ int check_common(const bb_decode_args* a, int64_t rows_per_group_max) {
     return fail(BB_ERR_SHAPE, "decode: heads must be a positive multiple of kv_heads");
   if (a->d <= 0 || a->d > 128 || a->d % 8) return fail(BB_ERR_UNSUPPORTED, "decode: head_dim must be a multiple of 8 and <= 128");
   if (a->cap <= 0) return fail(BB_ERR_SHAPE, "decode: empty cache");
+  if (a->cap > INT32_MAX) return fail(BB_ERR_UNSUPPORTED, "decode: cache capacity above 2^31 - 1 keys");
   if (a->n < 0 || a->n > a->cap) return fail(BB_ERR_ARG, "decode: n must lie in [0, cap]");
   if (a->heads / a->kv_heads > rows_per_group_max)
     return fail(BB_ERR_UNSUPPORTED, "decode: at most %d query heads per KV head", (int)rows_per_group_max);
@@ -398,7 +606,8 @@ int plan_decode(const bb_decode_args* a, DecodePlan* pl) {
   const int64_t rows = a->heads / rr;
   const int64_t total = a->front + a->window + a->route_k;
   int64_t splits = a->splits;
-  if (splits <= 0) splits = std::max<int64_t>(1, std::min<int64_t>(cdiv(total, (int64_t)4 * DK_BN), cdiv((int64_t)4 * num_sms(), rr)));
+  if (splits <= 0) splits = auto_splits(total, rr, dk_smem(dpad(a->d), true));
+  splits = std::min<int64_t>(splits, 8192);
   int64_t split_len = cdiv(cdiv(std::max<int64_t>(total, 1), splits), (int64_t)DK_BN) * DK_BN;
   splits = cdiv(std::max<int64_t>(total, 1), split_len);
   pl->splits = splits;
@@ -448,12 +657,11 @@ int launch_decode(const bb_decode_args* a, const DecodePlan& pl, char* ws, cudaS
   p.part_m = reinterpret_cast<float*>(ws);
   p.part_l = reinterpret_cast<float*>(ws + pl.m_bytes);
   p.part_acc = reinterpret_cast<float*>(ws + pl.m_bytes + pl.l_bytes);
-  const size_t smem = 4 * DkSmem<DP>::kv_bytes + (size_t)DK_MAXROWS * DP * 4 + (size_t)DK_MAXROWS * DK_BN * 4 +
-                      2 * DK_BN * 8;
+  const size_t smem = DkSmem<DP>::bytes(true);
   cudaFuncSetAttribute(decode_partial_kernel<T, DP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   decode_partial_kernel<T, DP><<<dim3((unsigned)rr, (unsigned)pl.splits), DK_THREADS, smem, stream>>>(p);
   BB_CHECK_LAUNCH("decode_partial_kernel");
-  decode_combine_kernel<T><<<(unsigned)cdiv(a->heads, (int64_t)4), 128, 0, stream>>>(p);
+  decode_combine_kernel<T><<<(unsigned)a->heads, 128, (size_t)pl.splits * 4, stream>>>(p);
   BB_CHECK_LAUNCH("decode_combine_kernel");
   return BB_OK;
 }
@@ -469,7 +677,8 @@ int plan_droute(const bb_decode_args* a, DroutePlan* pl) {
   if (a->route_k < 0 || a->route_k > a->cap) return fail(BB_ERR_ARG, "decode_route: k_route must lie in [0, cap]");
   int64_t splits = a->splits;
   if (splits <= 0)
-    splits = std::max<int64_t>(1, std::min<int64_t>({cdiv(a->cap, (int64_t)4 * DK_BN), cdiv((int64_t)4 * num_sms(), a->kv_heads), (int64_t)256}));
+    splits = auto_splits(a->cap, a->kv_heads, dk_smem(dpad(a->d), false));
+  splits = std::min<int64_t>(splits, 8192);
   int64_t split_len = cdiv(cdiv(a->cap, splits), (int64_t)DK_BN) * DK_BN;
   splits = cdiv(a->cap, split_len);
   pl->splits = splits;
@@ -492,11 +701,11 @@ int launch_droute(const bb_decode_args* a, const DroutePlan& pl, char* ws, cudaS
   p.part_m = reinterpret_cast<float*>(ws + pl.scores_bytes);
   p.part_l = reinterpret_cast<float*>(ws + pl.scores_bytes + pl.m_bytes);
   p.probs = a->out_probs ? a->out_probs : reinterpret_cast<float*>(ws + pl.scores_bytes + pl.m_bytes + pl.l_bytes);
-  const size_t smem = 2 * DkSmem<DP>::kv_bytes + (size_t)DK_MAXROWS * DP * 4 + 2 * DK_BN * 8;
+  const size_t smem = DkSmem<DP>::bytes(false);
   cudaFuncSetAttribute(droute_scores_kernel<T, DP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   droute_scores_kernel<T, DP><<<dim3((unsigned)a->kv_heads, (unsigned)pl.splits), DK_THREADS, smem, stream>>>(p);
   BB_CHECK_LAUNCH("droute_scores_kernel");
-  droute_pool_kernel<<<dim3((unsigned)a->kv_heads, (unsigned)cdiv(a->cap, (int64_t)256)), 256, 0, stream>>>(p);
+  droute_pool_kernel<<<dim3((unsigned)a->kv_heads, (unsigned)cdiv(a->cap, (int64_t)1024)), 256, 0, stream>>>(p);
   BB_CHECK_LAUNCH("droute_pool_kernel");
   if (a->route_k > 0 && a->out_idx) {
     int st = topk_sorted(p.probs, a->kv_heads, a->cap, a->route_k, a->out_idx, a->so_i, stream);
@@ -561,6 +770,18 @@ int decode_route(const bb_decode_args* a, void* ws, size_t ws_bytes, cudaStream_
   if (dp == 32) return launch_droute<__half, 32>(a, pl, w, stream);
   if (dp == 64) return launch_droute<__half, 64>(a, pl, w, stream);
   return launch_droute<__half, 128>(a, pl, w, stream);
+}
+
+int decode_fault_take(int* code) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, tc::g_tc_fault, sizeof(int));
+  if (e != cudaSuccess) return fail(BB_ERR_LAUNCH, "device_fault: %s", cudaGetErrorString(e));
+  if (v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(tc::g_tc_fault, &zero, sizeof(int));
+  }
+  *code = v;
+  return BB_OK;
 }
 
 }  // namespace bb

@@ -33,5 +33,6 @@ int flash_tc_splits(const bb_flash_args* a, int sms);
 // one for the attention kernels, one for the tcgen05 routing kernels.
 int flash_fault_take(int* code);
 int routes_fault_take(int* code);
+int decode_fault_take(int* code);
 
 }  // namespace bb
