@@ -146,3 +146,25 @@ def test_kv_evict_rejects_bad_arguments():
         _ops.kv_evict_(idx, col, k, k, sink=8, window=8, keep=64)           # keep > n - sink - window
     with pytest.raises(ValueError):
         _ops.kv_evict_(idx, col.double(), k, k, sink=8, window=8, keep=4)   # col must be fp32
+
+
+@pytest.mark.parametrize("n", [32768, 131072])
+def test_kv_evict_ties_take_lowest_positions(n):
+    """Column scores on four levels only (massive ties at the cut): the kept set equals the
+    oracle's exactly, ties resolved towards lower positions (the row-wise top-k runs as a cluster
+    of CTAs at these sizes, so this pins its cross-CTA tie order)."""
+    from utmist_bigger_bird_b200 import _ops
+    H, hk, d, budget, sink, w = 32, 8, 64, 512, 64, 4096
+    g = torch.Generator(device=DEV).manual_seed(11)
+    col = torch.floor(torch.rand(H, n, device=DEV, generator=g) * 4) * 2.5e-5
+    col[:, :sink] = -1
+    col[:, n - w:] = -1
+    idx = torch.stack([torch.randperm(n - sink - w, device=DEV, generator=g)[:budget] + sink for _ in range(H)])
+    idx = idx.sort(-1).values.to(torch.int32)
+    k = torch.randn(hk, n, d, device=DEV, generator=g).to(torch.bfloat16)
+    keep = 3000
+    kk, vv, pos = _ops.kv_evict_(idx, col, k, k, sink=sink, window=w, keep=keep)
+    torch.cuda.synchronize()
+    want, _ = orc.evict_positions(idx.cpu().numpy(), col.cpu().numpy(), kv_heads=hk, sink=sink, window=w,
+                                  evict_keep=keep)
+    assert np.array_equal(pos.cpu().numpy(), want)

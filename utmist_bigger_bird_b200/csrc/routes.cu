@@ -22,6 +22,9 @@
 #include "routes_tc.cuh"
 
 namespace bb {
+
+int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, int32_t* out, int64_t so_h,
+                cudaStream_t stream);
 namespace {
 
 constexpr int RT_THREADS = 256;   // 8 warps
@@ -593,11 +596,7 @@ int launch_routes_t(const bb_routes_args* a, const RtPlan& pl, char* ws, cudaStr
     route_col_kernel<T, DP><<<grid, RT_THREADS, smem, stream>>>(p);
     BB_CHECK_LAUNCH("route_col_kernel");
   }
-  if (a->budget > 0) {
-    route_topk_kernel<<<(unsigned)a->heads, TK_THREADS, 0, stream>>>(p.col, a->n, a->budget,
-                                                                    a->out_idx, a->so_h);
-    BB_CHECK_LAUNCH("route_topk_kernel");
-  }
+  if (a->budget > 0) return topk_sorted(p.col, a->heads, a->n, a->budget, a->out_idx, a->so_h, stream);
   return BB_OK;
 }
 
@@ -611,8 +610,8 @@ int launch_routes_d(const bb_routes_args* a, const RtPlan& pl, char* ws, cudaStr
 }  // namespace
 
 // The k largest of each of `rows` rows of n fp32 values, positions ascending (ties at the cut in
-// position order): the routing top-k, also used by KV eviction.
-int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, int32_t* out, int64_t so_h,
+// position order), one CTA a row: rows too long for the cluster kernel of topk.cu.
+int topk_single(const float* vals, int64_t rows, int64_t n, int64_t k, int32_t* out, int64_t so_h,
                 cudaStream_t stream) {
   if (k <= 0 || rows <= 0) return BB_OK;
   route_topk_kernel<<<(unsigned)rows, TK_THREADS, 0, stream>>>(vals, n, k, out, so_h);
