@@ -246,6 +246,25 @@ BB_API int bb_decode(const bb_decode_args* a, void* workspace, size_t workspace_
 BB_API int bb_decode_route_workspace_size(const bb_decode_args* a, size_t* bytes);
 BB_API int bb_decode_route(const bb_decode_args* a, void* workspace, size_t workspace_bytes, bb_stream_t stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Whole-model prefill memory path (the steps on either side of attention).
+ *
+ * bb_silu_mul replaces `act_fn(gate_proj(x)) * up_proj(x)` of the Llama MLP that
+ * modal_rd/mlp_chunk.py:19-26 runs chunk by chunk: gate <- act(gate) * up in place, rows x cols
+ * elements, row strides s_gate / s_up (elements). act(g) = g / (1 + exp(-g)) in fp32 rounded to
+ * the dtype, the product in fp32 rounded again: bit-identical to the two HF ops. dtype BB_BF16,
+ * BB_F16 or BB_F32.
+ *
+ * bb_embed_gather replaces CPUEmbedding.forward (modal_rd/cpu_embed.py:21-25): out[i] =
+ * table[ids[i]] for n int64 ids on the device, the [vocab, row_bytes] table in page-locked host
+ * memory (read by the kernel over the host link, no CPU gather or staging copy) or in device
+ * memory. Ids outside [0, vocab) give zero rows and add to *bad (a device int32 the caller zeroes
+ * and checks; the reference raises IndexError there). row_bytes a multiple of 16. */
+BB_API int bb_silu_mul(void* gate, int64_t s_gate, const void* up, int64_t s_up, int64_t rows, int64_t cols,
+                       int dtype, bb_stream_t stream);
+BB_API int bb_embed_gather(const void* table, int64_t vocab, int64_t row_bytes, const int64_t* ids, int64_t n,
+                           void* out, int32_t* bad, bb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -110,6 +110,8 @@ EXPORTS = {
     "bb_decode": (C.c_int, [C.POINTER(DecodeArgs), vp, C.c_size_t, vp]),
     "bb_decode_route_workspace_size": (C.c_int, [C.POINTER(DecodeArgs), C.POINTER(C.c_size_t)]),
     "bb_decode_route": (C.c_int, [C.POINTER(DecodeArgs), vp, C.c_size_t, vp]),
+    "bb_silu_mul": (C.c_int, [vp, i64, vp, i64, i64, i64, C.c_int, vp]),
+    "bb_embed_gather": (C.c_int, [vp, i64, i64, vp, i64, vp, vp, vp]),
 }
 
 _lib = None

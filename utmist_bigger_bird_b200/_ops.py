@@ -237,3 +237,46 @@ def decode_route_(q, k, *, front, window, scale, n=None, k_route=0, probs=None, 
     ws = _workspace(nbytes.value, q.device)
     _lib.check(L.bb_decode_route(C.byref(a), _ptr(ws), nbytes.value, _stream(q)), "bigger_bird_route")
     del keep
+
+
+def silu_mul_(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """gate <- act(gate) * up in place (SwiGLU of a Llama MLP chunk; bit-identical to HF's
+    ``act_fn(gate) * up``). gate/up: [..., I] CUDA tensors of one dtype, rows of stride >= I."""
+    if not gate.is_cuda or gate.dtype not in _DT or up.dtype != gate.dtype or up.device != gate.device:
+        raise ValueError("silu_mul_ requires CUDA gate/up of one dtype among fp16, bf16, fp32")
+    if gate.shape != up.shape:
+        raise ValueError(f"silu_mul_: shapes {tuple(gate.shape)} and {tuple(up.shape)} differ")
+    cols = gate.shape[-1]
+    g2, u2 = gate.reshape(-1, cols), up.reshape(-1, cols)
+    if g2.data_ptr() != gate.data_ptr() or g2.stride(-1) != 1 or u2.stride(-1) != 1:
+        raise ValueError("silu_mul_: gate must be viewable as rows with unit inner stride (in place)")
+    if g2.shape[0] > 1 and (g2.stride(0) < cols or u2.stride(0) < cols):
+        raise ValueError("silu_mul_: overlapping rows")
+    _lib.check(_lib.lib().bb_silu_mul(_ptr(g2), max(g2.stride(0), cols), _ptr(u2), max(u2.stride(0), cols),
+                                      g2.shape[0], cols, _DT[gate.dtype], _stream(gate)), "silu_mul")
+    return gate
+
+
+def embed_gather(table: torch.Tensor, ids: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Rows ``table[ids]`` gathered by a kernel on ``ids.device``; ``table`` may stay in page-locked
+    host memory (read over the host link) or be on that device. Raises IndexError for ids out of
+    range, like ``F.embedding``."""
+    if not ids.is_cuda or ids.dtype != torch.int64:
+        raise ValueError("embed_gather: ids must be a CUDA int64 tensor")
+    if table.dim() != 2 or not table.is_contiguous():
+        raise ValueError("embed_gather: table must be a contiguous [vocab, hidden] tensor")
+    if not table.is_cuda and not table.is_pinned():
+        raise ValueError("embed_gather: a host table must be pinned (page-locked)")
+    vocab, hidden = table.shape
+    ids_c = ids.contiguous()
+    if out is None:
+        out = torch.empty((*ids.shape, hidden), dtype=table.dtype, device=ids.device)
+    elif out.shape != (*ids.shape, hidden) or out.dtype != table.dtype or not out.is_contiguous():
+        raise ValueError("embed_gather: out must be a contiguous [*ids.shape, hidden] tensor of the table dtype")
+    bad = torch.zeros(1, dtype=torch.int32, device=ids.device)
+    _lib.check(_lib.lib().bb_embed_gather(_ptr(table), vocab, hidden * table.element_size(), _ptr(ids_c),
+                                          ids_c.numel(), _ptr(out), _ptr(bad), _stream(ids)), "embed_gather")
+    if int(bad.item()):
+        raise IndexError("index out of range in self")
+    return out
+

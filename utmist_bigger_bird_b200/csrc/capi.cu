@@ -57,6 +57,10 @@ int decode_route_workspace_size(const bb_decode_args* a, size_t* bytes);
 int decode_route(const bb_decode_args* a, void* ws, size_t ws_bytes, cudaStream_t stream);
 int flash_workspace_size(const bb_flash_args* a, size_t* bytes);
 int flash(const bb_flash_args* a, void* ws, size_t ws_bytes, cudaStream_t stream);
+int silu_mul(void* gate, int64_t s_gate, const void* up, int64_t s_up, int64_t rows, int64_t cols, int dtype,
+             cudaStream_t stream);
+int embed_gather(const void* table, int64_t vocab, int64_t row_bytes, const int64_t* ids, int64_t n, void* out,
+                 int32_t* bad, cudaStream_t stream);
 
 namespace {
 
@@ -211,6 +215,16 @@ int bb_decode_route_workspace_size(const bb_decode_args* a, size_t* bytes) {
 
 int bb_decode_route(const bb_decode_args* a, void* ws, size_t ws_bytes, bb_stream_t stream) {
   return bb::decode_route(a, ws, ws_bytes, bb::as_stream(stream));
+}
+
+int bb_silu_mul(void* gate, int64_t s_gate, const void* up, int64_t s_up, int64_t rows, int64_t cols, int dtype,
+                bb_stream_t stream) {
+  return bb::silu_mul(gate, s_gate, up, s_up, rows, cols, dtype, bb::as_stream(stream));
+}
+
+int bb_embed_gather(const void* table, int64_t vocab, int64_t row_bytes, const int64_t* ids, int64_t n, void* out,
+                    int32_t* bad, bb_stream_t stream) {
+  return bb::embed_gather(table, vocab, row_bytes, ids, n, out, bad, bb::as_stream(stream));
 }
 
 int bb_flash_workspace_size(const bb_flash_args* a, size_t* bytes) {
