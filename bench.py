@@ -541,6 +541,65 @@ def run_part(args):
           flush=True)
 
 
+def run_model(args):
+    """Whole-model prefill (config 4 shape, one GPU): a random-init 32-layer Llama-3-8B over
+    ``--model-tokens`` token ids, KV cache kept, logits of the last position only. Times the stock
+    Hugging Face model (dense SDPA, no memory savers) and then the same weights with the sparse
+    attention and the memory savers installed; prints one JSON line with both."""
+    from transformers import DynamicCache
+    from utmist_bigger_bird_b200 import (install, install_chunked_mlp, install_cpu_embedding,
+                                         install_inplace_residual)
+    from utmist_bigger_bird_b200.workload import make_llama
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n = args.model_tokens
+    model = make_llama(n_layers=args.model_layers, seed=2, device=dev)
+    g = torch.Generator(device="cpu").manual_seed(2)
+    ids = torch.randint(0, model.config.vocab_size, (1, n), generator=g).to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def measure():
+        def fwd():
+            with torch.inference_mode():
+                cache = DynamicCache(config=model.config)
+                out = model(input_ids=ids, past_key_values=cache, use_cache=True, logits_to_keep=1)
+                return out.logits, cache
+
+        logits, cache = fwd()  # warm-up
+        del cache
+        torch.cuda.synchronize(dev)
+        torch.cuda.empty_cache()
+        torch.cuda.reset_peak_memory_stats(dev)
+        base = torch.cuda.memory_allocated(dev)
+        times = []
+        for _ in range(max(1, args.steps)):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            logits, cache = fwd()
+            e.record(stream)
+            e.synchronize()
+            times.append(s.elapsed_time(e))
+            del cache
+        peak = torch.cuda.max_memory_allocated(dev) - base
+        ms = min(times)
+        return {"ms": ms, "tokens_per_s": n / (ms * 1e-3), "peak_extra_gb": peak / 1e9,
+                "weights_gb": base / 1e9}, logits.float()
+
+    stock, lg_dense = measure()
+    install(model, "vs", sink=64, window=16384, vertical=512, exact_tail=256)
+    install_chunked_mlp(model, 8192)
+    install_cpu_embedding(model)
+    install_inplace_residual(model)
+    ours, lg_sparse = measure()
+    top_dense, top_sparse = int(lg_dense[0, -1].argmax()), int(lg_sparse[0, -1].argmax())
+    print(json.dumps({"part": "model", "workload": f"config4 shape on 1 GPU: random-init Llama-3-8B x{args.model_layers} "
+                                                   f"layers, {n} tokens, KV cache kept, last-position logits",
+                      "stock_hf_dense": stock, "ours_sparse_savers": ours, "speedup": stock["ms"] / ours["ms"],
+                      "peak_ratio": ours["peak_extra_gb"] / max(stock["peak_extra_gb"], 1e-9),
+                      "next_token_dense": top_dense, "next_token_sparse": top_sparse,
+                      "gpu": torch.cuda.get_device_name(dev)}), flush=True)
+
+
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -549,10 +608,15 @@ def main():
     p.add_argument("--config", default="config2", choices=sorted(CONFIGS))
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    p.add_argument("--part", default="all", choices=["all", "decode", "evict"],
-                   help="time one side path alone (1 GPU) instead of the full benchmark")
+    p.add_argument("--part", default="all", choices=["all", "decode", "evict", "model"],
+                   help="time one side path alone (1 GPU) instead of the full benchmark; 'model' = the "
+                        "whole-model prefill with and without the sparse path and memory savers")
+    p.add_argument("--model-tokens", type=int, default=131072, help="--part model: prompt length")
+    p.add_argument("--model-layers", type=int, default=32, help="--part model: decoder layers")
     args = p.parse_args()
-    if args.part != "all":
+    if args.part == "model":
+        run_model(args)
+    elif args.part != "all":
         run_part(args)
     elif args.impl == "reference":
         run_reference(args)

@@ -17,7 +17,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-__all__ = ["LayerConfig", "CONFIGS", "rope_tables", "rope_reference_f32", "make_layer"]
+__all__ = ["LayerConfig", "CONFIGS", "rope_tables", "rope_reference_f32", "make_layer", "make_llama"]
 
 
 @dataclass(frozen=True)
@@ -122,3 +122,25 @@ def make_layer(cfg: LayerConfig, kv_heads=None, device="cpu"):
     if device != "cpu":
         q, k, v, cos, sin = (t.to(device) for t in (q, k, v, cos, sin))
     return q, k, v, cos, sin, planted
+
+
+def make_llama(n_layers: int = 32, seed: int = 2, device="cuda", dtype=torch.bfloat16):
+    """Random-init Llama-3-8B architecture (hidden 4096, 32 Q / 8 KV heads, head_dim 128, SwiGLU
+    14336, RMSNorm eps 1e-5, RoPE theta 500000, vocab 128256), weights ~ N(0, 0.02) from ``seed``:
+    the model of the whole-model prefill configs. Built directly on ``device`` in ``dtype``."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    cfg = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=n_layers,
+                      num_attention_heads=32, num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-5,
+                      rope_theta=500000.0, max_position_embeddings=1 << 20, initializer_range=0.02,
+                      tie_word_embeddings=False)
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(seed)
+    old = torch.get_default_dtype()
+    torch.set_default_dtype(dtype)
+    try:
+        with torch.device(device):
+            model = LlamaForCausalLM(cfg)
+    finally:
+        torch.set_default_dtype(old)
+    return model.eval()
+
