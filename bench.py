@@ -542,21 +542,35 @@ def run_part(args):
 
 
 def run_model(args):
-    """Whole-model prefill (config 4 shape, one GPU): a random-init 32-layer Llama-3-8B over
-    ``--model-tokens`` token ids, KV cache kept, logits of the last position only. Times the stock
-    Hugging Face model (dense SDPA, no memory savers) and then the same weights with the sparse
-    attention and the memory savers installed; prints one JSON line with both."""
+    """Whole-model prefill (config 4): a random-init 32-layer Llama-3-8B over ``--model-tokens``
+    token ids, KV cache kept, logits of the last position only. On one GPU: the stock Hugging Face
+    model (dense SDPA, no memory savers), then the same weights with the sparse attention and the
+    memory savers installed. Under torchrun (N GPUs): every rank holds the weights, attention is
+    head-sharded (``shard_llama``: the rank's KV heads and their query heads) and either
+    ``--model-shard gather`` (one NCCL all-gather a layer before a replicated o_proj, MLP replicated)
+    or ``tensor`` (row-parallel o_proj, tensor-parallel MLP, two all-reduces a layer); norms
+    replicated; the step time is the max over ranks.
+    Prints one JSON line (rank 0)."""
+    import torch.distributed as dist
     from transformers import DynamicCache
-    from utmist_bigger_bird_b200 import (install, install_chunked_mlp, install_cpu_embedding,
+    from utmist_bigger_bird_b200 import (install, install_chunked_mlp, install_cpu_embedding, install_fused_rmsnorm,
                                          install_inplace_residual)
+    from utmist_bigger_bird_b200.sharding import reduce_step, shard_llama
     from utmist_bigger_bird_b200.workload import make_llama
-    dev = torch.device("cuda", 0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
     n = args.model_tokens
     model = make_llama(n_layers=args.model_layers, seed=2, device=dev)
     g = torch.Generator(device="cpu").manual_seed(2)
     ids = torch.randint(0, model.config.vocab_size, (1, n), generator=g).to(dev)
     stream = torch.cuda.current_stream(dev)
+    attn = dict(sink=64, window=16384, vertical=512, exact_tail=256)
 
     def measure():
         def fwd():
@@ -573,6 +587,8 @@ def run_model(args):
         base = torch.cuda.memory_allocated(dev)
         times = []
         for _ in range(max(1, args.steps)):
+            if world > 1:
+                dist.barrier(device_ids=[local])
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record(stream)
             logits, cache = fwd()
@@ -581,23 +597,42 @@ def run_model(args):
             times.append(s.elapsed_time(e))
             del cache
         peak = torch.cuda.max_memory_allocated(dev) - base
-        ms = min(times)
-        return {"ms": ms, "tokens_per_s": n / (ms * 1e-3), "peak_extra_gb": peak / 1e9,
+        ms, _ = reduce_step(min(times), 0.0, dev)
+        pk, _ = reduce_step(peak / 1e9, 0.0, dev)
+        return {"ms": ms, "tokens_per_s": n / (ms * 1e-3), "peak_extra_gb_max_rank": pk,
                 "weights_gb": base / 1e9}, logits.float()
 
-    stock, lg_dense = measure()
-    install(model, "vs", sink=64, window=16384, vertical=512, exact_tail=256)
+    line = {"part": "model", "n_gpus": world,
+            "workload": f"config4 model: random-init Llama-3-8B x{args.model_layers} layers, {n} tokens, KV cache "
+                        f"kept, last-position logits" + (
+                            f"; attention head-sharded over {world} GPUs, " + (
+                                "all-gather before a replicated o_proj, MLP replicated" if args.model_shard == "gather"
+                                else "row-parallel o_proj and tensor-parallel MLP (two all-reduces a layer)")
+                            if world > 1 else "") + f"; RMSNorm {args.model_norm}",
+            "gpu": torch.cuda.get_device_name(dev)}
+    if world == 1:
+        stock, lg_dense = measure()
+        install(model, "vs", **attn)
+        line["stock_hf_dense"] = stock
+    else:
+        shard_llama(model, rank, world, mode=args.model_shard, **attn)
     install_chunked_mlp(model, 8192)
     install_cpu_embedding(model)
     install_inplace_residual(model)
+    if args.model_norm == "fused":
+        install_fused_rmsnorm(model)
     ours, lg_sparse = measure()
-    top_dense, top_sparse = int(lg_dense[0, -1].argmax()), int(lg_sparse[0, -1].argmax())
-    print(json.dumps({"part": "model", "workload": f"config4 shape on 1 GPU: random-init Llama-3-8B x{args.model_layers} "
-                                                   f"layers, {n} tokens, KV cache kept, last-position logits",
-                      "stock_hf_dense": stock, "ours_sparse_savers": ours, "speedup": stock["ms"] / ours["ms"],
-                      "peak_ratio": ours["peak_extra_gb"] / max(stock["peak_extra_gb"], 1e-9),
-                      "next_token_dense": top_dense, "next_token_sparse": top_sparse,
-                      "gpu": torch.cuda.get_device_name(dev)}), flush=True)
+    line["ours_sparse_savers"] = ours
+    if world == 1:
+        line["speedup"] = stock["ms"] / ours["ms"]
+        line["peak_ratio"] = ours["peak_extra_gb_max_rank"] / max(stock["peak_extra_gb_max_rank"], 1e-9)
+        line["next_token_dense"] = int(lg_dense[0, -1].argmax())
+    line["next_token_sparse"] = int(lg_sparse[0, -1].argmax())
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 def main():
@@ -613,6 +648,11 @@ def main():
                         "whole-model prefill with and without the sparse path and memory savers")
     p.add_argument("--model-tokens", type=int, default=131072, help="--part model: prompt length")
     p.add_argument("--model-layers", type=int, default=32, help="--part model: decoder layers")
+    p.add_argument("--model-norm", default="fused", choices=["fused", "chunked"],
+                   help="--part model: fused RMSNorm kernel (within 2 ulp of HF) or HF's norm in chunks (exact)")
+    p.add_argument("--model-shard", default="tensor", choices=["gather", "tensor"],
+                   help="--part model under torchrun: all-gather before a replicated o_proj and MLP, or "
+                        "row-parallel o_proj + tensor-parallel MLP")
     args = p.parse_args()
     if args.part == "model":
         run_model(args)

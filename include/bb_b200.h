@@ -265,6 +265,17 @@ BB_API int bb_silu_mul(void* gate, int64_t s_gate, const void* up, int64_t s_up,
 BB_API int bb_embed_gather(const void* table, int64_t vocab, int64_t row_bytes, const int64_t* ids, int64_t n,
                            void* out, int32_t* bad, bb_stream_t stream);
 
+/* bb_rmsnorm: y = weight * round(x * rsqrt(mean(x^2) + eps)) per row of `cols` elements, the
+ * LlamaRMSNorm arithmetic (HF modeling_llama: fp32 mean of squares, fp32 scale, rounded to the
+ * dtype, times the weight) with the fp32 sum in a different order (the normalised value within
+ * one ulp of HF's, the output within two). With `residual` non-NULL the row is first updated in
+ * place, x <- x + residual (rounded to the dtype, as torch's add_), which fuses the decoder
+ * layer's residual add
+ * (modal_rd/inplace_residual.py:23-25) with the norm that follows it. Row strides sx/sr/sy in
+ * elements; rows and strides 16-byte multiples. B200 extra (opt-in), not a reference entry. */
+BB_API int bb_rmsnorm(void* x, int64_t sx, const void* residual, int64_t sr, const void* weight, void* y, int64_t sy,
+                      int64_t rows, int64_t cols, float eps, int dtype, bb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

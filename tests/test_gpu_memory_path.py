@@ -191,3 +191,68 @@ def test_lower_prefill_peak():
         peaks.append(torch.cuda.max_memory_allocated() - base)
     saved = (peaks[0] - peaks[1]) / (16384 * 1024 * 2)
     assert saved >= 0.9, (peaks, saved)
+
+
+def test_shard_llama_single_rank_matches_install():
+    """shard_llama with one rank (q/k/v rows of all heads, o_proj through GatheredOProj) gives the
+    logits of the plain sparse install."""
+    from utmist_bigger_bird_b200.sharding import shard_llama
+    kw = dict(sink=4, window=64, vertical=16, exact_tail=8, block_m=16, block_n=16)
+    model = tiny(hidden=256, inter=512, heads=4)
+    ids = torch.randint(0, 512, (1, 300), device=DEV)
+    install(model, "vs", **kw)
+    with torch.inference_mode():
+        want = model(ids).logits
+    shard_llama(model, 0, 1, **kw)
+    with torch.inference_mode():
+        got = model(ids).logits
+    torch.testing.assert_close(got, want, atol=2e-2, rtol=2e-2)
+    assert (got.argmax(-1) == want.argmax(-1)).float().mean() > 0.99
+
+
+def _ulps(a, b):
+    """Distance in units of the last place between two bf16 tensors of the same sign pattern."""
+    ia = a.contiguous().view(torch.int16).to(torch.int32)
+    ib = b.contiguous().view(torch.int16).to(torch.int32)
+    return (ia - ib).abs()
+
+
+@pytest.mark.parametrize("n,hidden", [(300, 256), (4096, 4096), (17, 1024)])
+def test_fused_rmsnorm_within_one_ulp_of_hf(n, hidden):
+    """bb_rmsnorm against LlamaRMSNorm (bf16): the fp32 sum of squares runs in another order, so
+    the normalised value may move by one ulp before the weight multiply (at most two after it, for
+    weights above 1); almost all outputs are bit-identical."""
+    from transformers.models.llama.modeling_llama import LlamaRMSNorm
+    norm = LlamaRMSNorm(hidden, eps=1e-5).to(DEV, torch.bfloat16)
+    with torch.no_grad():
+        norm.weight.copy_(torch.randn(hidden, device=DEV) * 0.5 + 1)
+    x = torch.randn(1, n, hidden, device=DEV).to(torch.bfloat16)
+    want = norm(x)
+    got = _ops.rmsnorm_(x, norm.weight, norm.variance_epsilon)
+    u = _ulps(got, want)
+    assert int(u.max()) <= 2
+    assert (u == 0).float().mean() > 0.99
+    r = torch.randn_like(x)
+    x2 = x.clone()
+    want_x = x + r
+    want_y = norm(want_x)
+    got_y = _ops.rmsnorm_(x2, norm.weight, norm.variance_epsilon, residual=r)
+    assert torch.equal(x2, want_x), "residual add in place, rounded like torch"
+    assert int(_ulps(got_y, want_y).max()) <= 2
+
+
+def test_fused_rmsnorm_model_close_to_hf():
+    """install_fused_rmsnorm + install_inplace_residual (fused residual add) on a tiny Llama: the
+    prefill and decode logits stay within bf16 noise of the unfused model and pick the same tokens
+    almost everywhere."""
+    from utmist_bigger_bird_b200 import install_fused_rmsnorm
+    model = tiny(hidden=256, inter=512, heads=4)
+    ids = torch.randint(0, 512, (1, 300), device=DEV)
+    want = _run(model, ids)
+    install_inplace_residual(model)
+    install_fused_rmsnorm(model)
+    install_fused_rmsnorm(model)
+    got = _run(model, ids)
+    a, b = got[0][0], want[0][0]
+    assert (a - b).abs().max() < 0.1
+    assert (a.argmax(-1) == b.argmax(-1)).float().mean() > 0.97

@@ -16,7 +16,8 @@ from .bigger_bird_route import bigger_bird_route, pooled_probs  # noqa: F401
 from .cpu_embed import CPUEmbedding, install_cpu_embedding  # noqa: F401
 from .inplace_residual import install_inplace_residual  # noqa: F401
 from .mlp_chunk import install_chunked_mlp  # noqa: F401
+from .rmsnorm import install_fused_rmsnorm  # noqa: F401
 
 __all__ = ["RDAttention", "install", "rope_inplace", "vertical_budget", "forward_pool", "bigger_bird_flash",
            "bigger_bird_decode", "bigger_bird_route", "pooled_probs", "CPUEmbedding", "install_cpu_embedding",
-           "install_inplace_residual", "install_chunked_mlp"]
+           "install_inplace_residual", "install_chunked_mlp", "install_fused_rmsnorm"]

@@ -112,6 +112,7 @@ EXPORTS = {
     "bb_decode_route": (C.c_int, [C.POINTER(DecodeArgs), vp, C.c_size_t, vp]),
     "bb_silu_mul": (C.c_int, [vp, i64, vp, i64, i64, i64, C.c_int, vp]),
     "bb_embed_gather": (C.c_int, [vp, i64, i64, vp, i64, vp, vp, vp]),
+    "bb_rmsnorm": (C.c_int, [vp, i64, vp, i64, vp, vp, i64, i64, i64, C.c_float, C.c_int, vp]),
 }
 
 _lib = None

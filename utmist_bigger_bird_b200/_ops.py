@@ -280,3 +280,32 @@ def embed_gather(table: torch.Tensor, ids: torch.Tensor, *, out: torch.Tensor | 
         raise IndexError("index out of range in self")
     return out
 
+
+
+def rmsnorm_(x: torch.Tensor, weight: torch.Tensor, eps: float, *, residual: torch.Tensor | None = None,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """``weight * round(x * rsqrt(mean(x^2) + eps))`` over the last dim (LlamaRMSNorm's arithmetic,
+    fp32 sum in a different order). With ``residual``, ``x += residual`` in place first (the
+    decoder layer's residual add, fused)."""
+    if not x.is_cuda or x.dtype not in _DT or weight.dtype != x.dtype or weight.device != x.device:
+        raise ValueError("rmsnorm_ requires CUDA x and weight of one dtype among fp16, bf16, fp32")
+    cols = x.shape[-1]
+    if weight.shape != (cols,) or not weight.is_contiguous():
+        raise ValueError("rmsnorm_: weight must be a contiguous [hidden] vector")
+    x2 = x.reshape(-1, cols)
+    if x2.data_ptr() != x.data_ptr() or x2.stride(-1) != 1:
+        raise ValueError("rmsnorm_: x must be viewable as rows with unit inner stride")
+    r2 = None
+    if residual is not None:
+        if residual.shape != x.shape or residual.dtype != x.dtype:
+            raise ValueError("rmsnorm_: residual must match x")
+        r2 = residual.reshape(-1, cols)
+    if out is None:
+        out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    y2 = out.reshape(-1, cols)
+    rows = x2.shape[0]
+    _lib.check(_lib.lib().bb_rmsnorm(_ptr(x2), x2.stride(0) if rows > 1 else cols, _ptr(r2),
+                                     (r2.stride(0) if rows > 1 else cols) if r2 is not None else 0,
+                                     _ptr(weight), _ptr(y2), y2.stride(0) if rows > 1 else cols, rows, cols,
+                                     float(eps), _DT[x.dtype], _stream(x)), "rmsnorm")
+    return out

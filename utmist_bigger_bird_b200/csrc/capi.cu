@@ -61,6 +61,8 @@ int silu_mul(void* gate, int64_t s_gate, const void* up, int64_t s_up, int64_t r
              cudaStream_t stream);
 int embed_gather(const void* table, int64_t vocab, int64_t row_bytes, const int64_t* ids, int64_t n, void* out,
                  int32_t* bad, cudaStream_t stream);
+int rmsnorm(void* x, int64_t sx, const void* r, int64_t sr, const void* w, void* y, int64_t sy, int64_t rows,
+            int64_t cols, float eps, int dtype, cudaStream_t stream);
 
 namespace {
 
@@ -225,6 +227,11 @@ int bb_silu_mul(void* gate, int64_t s_gate, const void* up, int64_t s_up, int64_
 int bb_embed_gather(const void* table, int64_t vocab, int64_t row_bytes, const int64_t* ids, int64_t n, void* out,
                     int32_t* bad, bb_stream_t stream) {
   return bb::embed_gather(table, vocab, row_bytes, ids, n, out, bad, bb::as_stream(stream));
+}
+
+int bb_rmsnorm(void* x, int64_t sx, const void* residual, int64_t sr, const void* weight, void* y, int64_t sy,
+               int64_t rows, int64_t cols, float eps, int dtype, bb_stream_t stream) {
+  return bb::rmsnorm(x, sx, residual, sr, weight, y, sy, rows, cols, eps, dtype, bb::as_stream(stream));
 }
 
 int bb_flash_workspace_size(const bb_flash_args* a, size_t* bytes) {

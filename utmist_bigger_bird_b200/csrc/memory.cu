@@ -12,8 +12,11 @@
 //                        21-25 gathers on the CPU, then copies into pinned staging, then to the
 //                        GPU). Ids out of range are counted (the caller raises) and give zero rows.
 //
-// Both are bound by bytes moved: silu_mul by HBM (3 reads/writes of the chunk), embed_gather by the
-// host link (n * row_bytes).
+//   rmsnorm_kernel       RMSNorm (optionally fused with the residual add before it) for the B200
+//                        model path; HF's arithmetic, the fp32 sum of squares in a different order.
+//
+// All are bound by bytes moved: silu_mul and rmsnorm by HBM, embed_gather by the host link
+// (n * row_bytes).
 #include "bb_common.cuh"
 
 namespace bb {
@@ -73,6 +76,56 @@ __global__ void embed_gather_kernel(const uint4* __restrict__ table, int64_t voc
   }
 }
 
+// RMSNorm of one row per warp (optionally after an in-place residual add x <- x + r, rounded to
+// the dtype as torch's add_ does): y = w * round(x * rsqrt(mean(x^2) + eps)) with the mean
+// accumulated in fp32 (HF LlamaRMSNorm's arithmetic; only the order of the fp32 sum differs).
+// The second pass re-reads each lane's own vectors (L1 hits); x is read from HBM once.
+template <typename T>
+__global__ void __launch_bounds__(256) rmsnorm_kernel(T* __restrict__ x, int64_t sx, const T* __restrict__ r,
+                                                      int64_t sr, const T* __restrict__ w, T* __restrict__ y,
+                                                      int64_t sy, int64_t rows, int64_t cols, float eps) {
+  constexpr int V = 16 / sizeof(T);
+  const int lane = threadIdx.x % 32;
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  if (row >= rows) return;
+  T* xr = x + row * sx;
+  const T* rr = r ? r + row * sr : nullptr;
+  T* yr = y + row * sy;
+  const int64_t nvec = cols / V;
+  float acc = 0.f;
+  for (int64_t v = lane; v < nvec; v += 32) {
+    uint4 xv = *reinterpret_cast<const uint4*>(xr + v * V);
+    T* xe = reinterpret_cast<T*>(&xv);
+    if (rr) {
+      const uint4 rv = *reinterpret_cast<const uint4*>(rr + v * V);
+      const T* re = reinterpret_cast<const T*>(&rv);
+#pragma unroll
+      for (int e = 0; e < V; ++e) xe[e] = Elem<T>::from_f(Elem<T>::to_f(xe[e]) + Elem<T>::to_f(re[e]));
+      *reinterpret_cast<uint4*>(xr + v * V) = xv;
+    }
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      const float f = Elem<T>::to_f(xe[e]);
+      acc = fmaf(f, f, acc);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  const float inv = rsqrtf(acc / (float)cols + eps);
+  for (int64_t v = lane; v < nvec; v += 32) {
+    const uint4 xv = *reinterpret_cast<const uint4*>(xr + v * V);  // this lane's own vector (L1 hit)
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + v * V);
+    uint4 yv;
+    const T* xe = reinterpret_cast<const T*>(&xv);
+    const T* we = reinterpret_cast<const T*>(&wv);
+    T* ye = reinterpret_cast<T*>(&yv);
+#pragma unroll
+    for (int e = 0; e < V; ++e)
+      ye[e] = Elem<T>::from_f(Elem<T>::to_f(we[e]) * Elem<T>::round(Elem<T>::to_f(xe[e]) * inv));
+    *reinterpret_cast<uint4*>(yr + v * V) = yv;
+  }
+}
+
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 template <typename T>
@@ -107,6 +160,38 @@ int silu_mul(void* gate, int64_t s_gate, const void* up, int64_t s_up, int64_t r
     case BB_F32: return launch_silu_mul<float>(gate, s_gate, up, s_up, rows, cols, stream);
     default: return fail(BB_ERR_DTYPE, "silu_mul: dtype must be bf16, f16 or f32");
   }
+}
+
+int rmsnorm(void* x, int64_t sx, const void* r, int64_t sr, const void* w, void* y, int64_t sy, int64_t rows,
+            int64_t cols, float eps, int dtype, cudaStream_t stream) {
+  if (rows < 0 || cols <= 0) return fail(BB_ERR_SHAPE, "rmsnorm: bad shape");
+  if (rows == 0) return BB_OK;
+  if (!x || !w || !y) return fail(BB_ERR_ARG, "rmsnorm: null pointer");
+  const int es = dtype == BB_F32 ? 4 : 2;
+  if (dtype != BB_BF16 && dtype != BB_F16 && dtype != BB_F32) return fail(BB_ERR_DTYPE, "rmsnorm: dtype must be bf16, f16 or f32");
+  if ((cols * es) % 16 || (sx * es) % 16 || (sy * es) % 16 || (r && (sr * es) % 16) || !al16(x) || !al16(w) ||
+      !al16(y) || (r && !al16(r)))
+    return fail(BB_ERR_STRIDE, "rmsnorm: rows must be 16-byte multiples on 16-byte boundaries");
+  if (sx < cols || sy < cols || (r && sr < cols)) return fail(BB_ERR_STRIDE, "rmsnorm: row stride below the row length");
+  const unsigned blocks = (unsigned)cdiv(rows, 8);
+  switch (dtype) {
+    case BB_BF16:
+      rmsnorm_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(
+          static_cast<__nv_bfloat16*>(x), sx, static_cast<const __nv_bfloat16*>(r), sr,
+          static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y), sy, rows, cols, eps);
+      break;
+    case BB_F16:
+      rmsnorm_kernel<__half><<<blocks, 256, 0, stream>>>(static_cast<__half*>(x), sx, static_cast<const __half*>(r), sr,
+                                                          static_cast<const __half*>(w), static_cast<__half*>(y), sy,
+                                                          rows, cols, eps);
+      break;
+    default:
+      rmsnorm_kernel<float><<<blocks, 256, 0, stream>>>(static_cast<float*>(x), sx, static_cast<const float*>(r), sr,
+                                                         static_cast<const float*>(w), static_cast<float*>(y), sy,
+                                                         rows, cols, eps);
+  }
+  BB_CHECK_LAUNCH("rmsnorm_kernel");
+  return BB_OK;
 }
 
 int embed_gather(const void* table, int64_t vocab, int64_t row_bytes, const int64_t* ids, int64_t n, void* out,

@@ -23,9 +23,14 @@ def _forward(self, hidden_states, attention_mask=None, position_ids=None, past_k
     h, _ = self.self_attn(hidden_states=h, attention_mask=attention_mask, position_ids=position_ids,
                           past_key_values=past_key_values, use_cache=use_cache,
                           position_embeddings=position_embeddings, **kwargs)
-    hidden_states.add_(h)
+    fused = getattr(self.post_attention_layernorm, "fused_add", None)  # install_fused_rmsnorm
+    if fused is not None:
+        normed = fused(hidden_states, h)
+    else:
+        hidden_states.add_(h)
+        normed = self.post_attention_layernorm(hidden_states)
     del h
-    hidden_states.add_(self.mlp(self.post_attention_layernorm(hidden_states)))
+    hidden_states.add_(self.mlp(normed))
     return hidden_states
 
 

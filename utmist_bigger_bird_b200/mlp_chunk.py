@@ -25,6 +25,8 @@ __all__ = ["install_chunked_mlp"]
 
 
 def _is_swiglu(mlp) -> bool:
+    # gate/up/down with a `weight` and no bias (nn.Linear, or the tensor-parallel blocks of
+    # sharding.shard_llama, whose down projection sums over the ranks in `all_reduce_`).
     projs = [getattr(mlp, n, None) for n in ("gate_proj", "up_proj", "down_proj")]
     if any(p is None or getattr(p, "bias", None) is not None or not hasattr(p, "weight") for p in projs):
         return False
@@ -55,7 +57,8 @@ def _swiglu_chunked(mlp, chunk: int, base):
             torch.matmul(xs, wu.t(), out=u)
             _ops.silu_mul_(g, u)
             torch.matmul(g, wd.t(), out=out[..., s:e, :])
-        return out
+        reduce = getattr(_mlp.down_proj, "all_reduce_", None)  # tensor-parallel down projection
+        return reduce(out) if reduce is not None else out
 
     return forward
 
