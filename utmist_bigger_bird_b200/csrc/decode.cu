@@ -562,6 +562,476 @@ __global__ void __launch_bounds__(256) droute_pool_kernel(DecodeParams p) {
   }
 }
 
+// ----------------------------------------------------------------------------- TMA variant
+// Head dim 128 with each head's cache rows evenly strided (the [Hkv, cap, d] layout of a KV
+// cache): a producer warp fills each 64-key stage either with four tiled TMA loads (K and V x two
+// 64-column halves, 128-byte swizzle) when the stage's 64 positions are consecutive cache rows
+// (front, window and dense stages), or with cp.async 16-byte chunks into the same swizzled
+// layout (stages with routed or missing keys). Split s takes stages s, s + S, s + 2S, ... of the
+// virtual key list (S splits), so the few routed stages spread over many CTAs instead of lining up
+// in the last one. Four consumer warps compute as in the generic kernel on the swizzled tiles.
+constexpr int DT_CONSUMERS = 4;
+constexpr int DT_THREADS = 32 * (DT_CONSUMERS + 1);
+constexpr int DT_NST = 3;
+constexpr uint32_t DT_HALF = 64u * 128u;   // 64 rows x 128 bytes: one 64-column half
+constexpr uint32_t DT_TILE = 2u * DT_HALF;  // 64 rows x 128 columns of K (or V)
+constexpr int DT_LDQ = 136;                 // padded query rows (elements)
+
+struct DtMaps {
+  CUtensorMap k, v;           // 2-D row views [rows, 128]; head h starts at row h * head_rows
+  int64_t k_head_rows, v_head_rows;
+};
+
+struct DtSmem {
+  static constexpr uint32_t ring(bool with_v) { return DT_NST * DT_TILE * (with_v ? 2u : 1u); }
+  static constexpr uint32_t merge = DT_CONSUMERS * DK_MAXROWS * (128 + 2) * 4;
+  static constexpr uint32_t area(bool with_v) { return ring(with_v) > merge ? ring(with_v) : merge; }
+  static constexpr uint32_t q_bytes = DK_MAXROWS * DT_LDQ * 2;
+  static constexpr uint32_t ctl = DT_NST * 8 * 3 + 16;
+  static constexpr size_t bytes(bool with_v) { return (size_t)area(with_v) + q_bytes + ctl + 1024; }  // + alignment
+};
+
+template <typename T> __device__ __forceinline__ void zero_row(T* row, int64_t d) {
+  for (int64_t c = 0; c < d; c += 8) *reinterpret_cast<uint4*>(row + c) = make_uint4(0u, 0u, 0u, 0u);
+}
+
+__device__ __forceinline__ uint32_t sw_addr(uint32_t tile, int row, int chunk) {
+  return tile + (uint32_t)(chunk >> 3) * DT_HALF + (uint32_t)row * 128u + ((uint32_t)((chunk & 7) ^ (row & 7)) << 4);
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar) : "memory");
+}
+
+// One stage: positions p0 / p1 of rows `lane` / `lane + 32` (-1: not a key). A stage of 64
+// consecutive cache rows is two (K) or four (K and V) tiled TMA loads; any other stage (routed
+// keys, the cache's edges) is cp.async 16-byte chunks into the same 128B-swizzled layout, rows that
+// are not keys zero-filled, completion through cp.async.mbarrier.arrive. The stage's full barrier
+// expects 33 arrivals: every producer lane once, plus lane 0 once more after it has published the
+// key mask (a release the consumers' wait acquires).
+template <typename T>
+__device__ __forceinline__ void dt_produce(uint64_t* mask_slot, uint32_t bar, int32_t p0, int32_t p1,
+                                           const CUtensorMap* mk, const CUtensorMap* mv, int64_t k_row0,
+                                           int64_t v_row0, const T* K, int64_t sk_t, const T* V, int64_t sv_t,
+                                           uint32_t ktile, uint32_t vtile) {
+  const int lane = threadIdx.x % 32;
+  const unsigned m0 = __ballot_sync(0xffffffffu, p0 >= 0), m1 = __ballot_sync(0xffffffffu, p1 >= 0);
+  const int32_t first = __shfl_sync(0xffffffffu, p0, 0);
+  const bool contiguous =
+      __all_sync(0xffffffffu, p0 >= 0 && p1 >= 0 && p0 == first + lane && p1 == first + 32 + lane);
+  if (lane == 0) *mask_slot = ((uint64_t)m1 << 32) | m0;
+  if (contiguous) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier cp.async fills of the slot first
+    __syncwarp();
+    if (lane == 0) {
+      tc::mbar_expect_tx(bar, mv ? 2u * DT_TILE : DT_TILE);
+      tma_load_2d(ktile, mk, 0, (int)(k_row0 + first), bar);
+      tma_load_2d(ktile + DT_HALF, mk, 64, (int)(k_row0 + first), bar);
+      if (mv) {
+        tma_load_2d(vtile, mv, 0, (int)(v_row0 + first), bar);
+        tma_load_2d(vtile + DT_HALF, mv, 64, (int)(v_row0 + first), bar);
+      }
+    }
+    tc::mbar_arrive(bar);
+  } else {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = lane + 32 * h;
+      const int32_t pos = h ? p1 : p0;
+      const bool ok = pos >= 0;
+      const T* kr = K + (int64_t)(ok ? pos : 0) * sk_t;
+      const T* vr = mv ? V + (int64_t)(ok ? pos : 0) * sv_t : nullptr;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        cp_async_16(sw_addr(ktile, row, c), kr + c * 8, ok);
+        if (vr) cp_async_16(sw_addr(vtile, row, c), vr + c * 8, ok);
+      }
+    }
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+    if (lane == 0) tc::mbar_arrive(bar);
+  }
+}
+
+// S = Q K^T for this warp's 16 keys of a swizzled K tile (two accumulator chains, as warp_scores).
+template <typename T>
+__device__ __forceinline__ void dt_scores(const uint32_t (&qf)[8][4], uint32_t kt, int key0, float (&s)[2][4]) {
+  const int lane = threadIdx.x % 32;
+  float e[2][4], o[2][4];
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) e[t][i] = o[t][i] = 0.f;
+  const int row = key0 + (lane / 16) * 8 + (lane % 8);
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    uint32_t b0, b1, b2, b3;
+    ldmatrix_x4(b0, b1, b2, b3, sw_addr(kt, row, kk * 2 + (lane / 8) % 2));
+    const uint32_t bA[2] = {b0, b1}, bB[2] = {b2, b3};
+    float(&a0)[4] = (kk & 1) ? o[0] : e[0];
+    float(&a1)[4] = (kk & 1) ? o[1] : e[1];
+    mma_16816<T>(a0, qf[kk], bA);
+    mma_16816<T>(a1, qf[kk], bB);
+  }
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) s[t][i] = e[t][i] + o[t][i];
+}
+
+struct DtCtl {
+  uint64_t* mask;
+  uint64_t* full;
+  uint64_t* empty;
+  volatile uint32_t* abort_flag;
+};
+
+template <typename T>
+__device__ __forceinline__ void dt_setup(unsigned char* smem_raw, bool with_v, uint32_t& ring, T*& qs, DtCtl& c) {
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t pad = ((raw + 1023u) & ~1023u) - raw;  // the swizzled TMA tiles need 1024-byte alignment
+  unsigned char* base = smem_raw + pad;
+  ring = raw + pad;
+  qs = reinterpret_cast<T*>(base + DtSmem::area(with_v));
+  unsigned char* ctl = base + DtSmem::area(with_v) + DtSmem::q_bytes;
+  c.mask = reinterpret_cast<uint64_t*>(ctl);
+  c.full = c.mask + DT_NST;
+  c.empty = c.full + DT_NST;
+  c.abort_flag = reinterpret_cast<volatile uint32_t*>(c.empty + DT_NST);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < DT_NST; ++i) {
+      tc::mbar_init(smem_u32(c.full + i), 33);
+      tc::mbar_init(smem_u32(c.empty + i), DT_CONSUMERS);
+    }
+    *c.abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void dt_load_q(const DecodeParams& p, int64_t first_head, int rows, T* qs) {
+  const T* Q = static_cast<const T*>(p.q);
+  for (int i = threadIdx.x; i < DK_MAXROWS * 128; i += DT_THREADS) {
+    const int row = i / 128, col = i % 128;
+    qs[row * DT_LDQ + col] = row < rows ? Q[(first_head + row) * p.sq_h + col] : Elem<T>::from_f(0.f);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void dt_q_frags(const T* qs, uint32_t (&qf)[8][4]) {
+  const int lane = threadIdx.x % 32;
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+    ldmatrix_x4(qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3],
+                smem_u32(qs + (lane % 16) * DT_LDQ + kk * 16 + (lane / 16) * 8));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(DT_THREADS, 2) decode_tma_kernel(const __grid_constant__ DtMaps maps, DecodeParams p) {
+  extern __shared__ unsigned char smem_raw[];
+  uint32_t ring;
+  T* qs;
+  DtCtl c;
+  dt_setup<T>(smem_raw, true, ring, qs, c);
+  const int64_t r = blockIdx.x, split = blockIdx.y;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t n = cache_len(p);
+  const int rows = (int)p.rows;
+  const int64_t kv = (r * p.rows) / p.groups;
+  const int64_t total = p.front + p.window + p.route_k;
+  const int64_t stages = cdiv(total, (int64_t)DK_BN);
+  const int nblocks = split < stages ? (int)cdiv(stages - split, p.splits) : 0;  // stages split + i * splits
+  dt_load_q<T>(p, r * p.rows, rows, qs);
+  __syncthreads();
+
+  float o[16][4];
+  float m0 = -1.0e20f, m1 = -1.0e20f, l0 = 0.f, l1 = 0.f;
+  if (warp == DT_CONSUMERS) {
+    const T* K = static_cast<const T*>(p.k) + kv * p.sk_h;
+    const T* V = static_cast<const T*>(p.v) + kv * p.sv_h;
+    auto fetch = [&](int blk, int row) -> int32_t {
+      const int64_t j = (split + (int64_t)blk * p.splits) * DK_BN + row;
+      return (blk < nblocks && j < total) ? (int32_t)virtual_pos(p, r, j, n) : -1;
+    };
+    int32_t f0 = fetch(0, lane), f1 = fetch(0, lane + 32);
+    int slot = 0;
+    uint32_t ph = 0;
+    for (int blk = 0; blk < nblocks; ++blk) {
+      if (blk >= DT_NST && !tc::mbar_wait_warp(smem_u32(c.empty + slot), ph ^ 1u, c.abort_flag, 44)) break;
+      const int32_t p0 = f0, p1 = f1;
+      f0 = fetch(blk + 1, lane);
+      f1 = fetch(blk + 1, lane + 32);
+      const uint32_t off = (uint32_t)slot * 2u * DT_TILE;
+      dt_produce<T>(c.mask + slot, smem_u32(c.full + slot), p0, p1, &maps.k, &maps.v, kv * maps.k_head_rows,
+                    kv * maps.v_head_rows, K, p.sk_t, V, p.sv_t, ring + off, ring + off + DT_TILE);
+      if (++slot == DT_NST) {
+        slot = 0;
+        ph ^= 1u;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    uint32_t qf[8][4];
+    dt_q_frags<T>(qs, qf);
+    const int key0 = warp * 16;
+    const bool two = rows > 8;
+    const int kbit = key0 + 2 * (lane % 4);
+    const int vrow = key0 + ((lane / 8) % 2) * 8 + (lane % 8);
+    int slot = 0;
+    uint32_t ph = 0;
+    for (int b = 0; b < nblocks; ++b) {
+      if (!tc::mbar_wait_warp(smem_u32(c.full + slot), ph, c.abort_flag, 45)) break;
+      const uint64_t msk = c.mask[slot];
+      const uint32_t kt = ring + (uint32_t)slot * 2u * DT_TILE, vt = kt + DT_TILE;
+      float s[2][4];
+      dt_scores<T>(qf, kt, key0, s);
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const bool v0 = (msk >> (kbit + t * 8)) & 1u, v1 = (msk >> (kbit + t * 8 + 1)) & 1u;
+        s[t][0] = v0 ? s[t][0] * p.scale_log2 : -INFINITY;
+        s[t][1] = v1 ? s[t][1] * p.scale_log2 : -INFINITY;
+        s[t][2] = v0 ? s[t][2] * p.scale_log2 : -INFINITY;
+        s[t][3] = v1 ? s[t][3] * p.scale_log2 : -INFINITY;
+        mx0 = fmaxf(mx0, fmaxf(s[t][0], s[t][1]));
+        mx1 = fmaxf(mx1, fmaxf(s[t][2], s[t][3]));
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      const float n0 = fmaxf(m0, mx0);
+      const float a0 = fast_exp2(m0 - n0);
+      m0 = n0;
+      float pr[2][4];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        pr[t][0] = fast_exp2(s[t][0] - n0);
+        pr[t][1] = fast_exp2(s[t][1] - n0);
+        pr[t][2] = pr[t][3] = 0.f;
+      }
+      float a1 = 1.f;
+      if (two) {
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float n1 = fmaxf(m1, mx1);
+        a1 = fast_exp2(m1 - n1);
+        m1 = n1;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          pr[t][2] = fast_exp2(s[t][2] - n1);
+          pr[t][3] = fast_exp2(s[t][3] - n1);
+        }
+        l1 = l1 * a1 + (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
+      }
+      l0 = l0 * a0 + (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
+      const uint32_t a[4] = {pack2<T>(pr[0][0], pr[0][1]), pack2<T>(pr[0][2], pr[0][3]),
+                             pack2<T>(pr[1][0], pr[1][1]), pack2<T>(pr[1][2], pr[1][3])};
+      if (!__all_sync(0xffffffffu, a0 == 1.f && a1 == 1.f)) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          o[i][0] *= a0;
+          o[i][1] *= a0;
+          o[i][2] *= a1;
+          o[i][3] *= a1;
+        }
+      }
+#pragma unroll
+      for (int dp = 0; dp < 8; ++dp) {
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(b0, b1, b2, b3, sw_addr(vt, vrow, dp * 2 + lane / 16));
+        const uint32_t bA[2] = {b0, b1}, bB[2] = {b2, b3};
+        mma_16816<T>(o[dp * 2], a, bA);
+        mma_16816<T>(o[dp * 2 + 1], a, bB);
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(smem_u32(c.empty + slot));
+      if (++slot == DT_NST) {
+        slot = 0;
+        ph ^= 1u;
+      }
+    }
+  }
+  __syncthreads();
+  if (*c.abort_flag) {
+    if (warp == DT_CONSUMERS && lane == 0)
+      for (int blk = max(0, nblocks - DT_NST); blk < nblocks; ++blk)
+        tc::mbar_drain(smem_u32(c.full + blk % DT_NST), (uint32_t)((blk / DT_NST) & 1));
+    return;
+  }
+  const uint32_t pad = ring - smem_u32(smem_raw);
+  float* wm = reinterpret_cast<float*>(smem_raw + pad);
+  float* wl = wm + DT_CONSUMERS * DK_MAXROWS;
+  float* wo = wl + DT_CONSUMERS * DK_MAXROWS;
+  if (warp < DT_CONSUMERS) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    const int g = lane / 4, cc = 2 * (lane % 4);
+    if (lane % 4 == 0) {
+      wm[warp * DK_MAXROWS + g] = m0;
+      wl[warp * DK_MAXROWS + g] = l0;
+      wm[warp * DK_MAXROWS + g + 8] = m1;
+      wl[warp * DK_MAXROWS + g + 8] = l1;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      *reinterpret_cast<float2*>(wo + (warp * DK_MAXROWS + g) * 128 + i * 8 + cc) = make_float2(o[i][0], o[i][1]);
+      *reinterpret_cast<float2*>(wo + (warp * DK_MAXROWS + g + 8) * 128 + i * 8 + cc) = make_float2(o[i][2], o[i][3]);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < rows * 128; i += DT_THREADS) {
+    const int row = i / 128, col = i % 128;
+    float M = -1.0e20f;
+#pragma unroll
+    for (int w = 0; w < DT_CONSUMERS; ++w) M = fmaxf(M, wm[w * DK_MAXROWS + row]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < DT_CONSUMERS; ++w) {
+      const float f = fast_exp2(wm[w * DK_MAXROWS + row] - M);
+      L += wl[w * DK_MAXROWS + row] * f;
+      A += wo[(w * DK_MAXROWS + row) * 128 + col] * f;
+    }
+    const int64_t at = (r * p.splits + split) * p.rows + row;
+    if (col == 0) {
+      p.part_m[at] = M;
+      p.part_l[at] = L;
+    }
+    p.part_acc[at * 128 + col] = A;
+  }
+}
+
+// Decode routing pass 1 on the TMA path: K stages only (contiguous positions, so every full stage
+// is one pair of tiled loads).
+template <typename T>
+__global__ void __launch_bounds__(DT_THREADS) droute_tma_kernel(const __grid_constant__ DtMaps maps, DecodeParams p) {
+  extern __shared__ unsigned char smem_raw[];
+  uint32_t ring;
+  T* qs;
+  DtCtl c;
+  dt_setup<T>(smem_raw, false, ring, qs, c);
+  const int64_t kv = blockIdx.x, split = blockIdx.y;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t n = cache_len(p);
+  const int rows = (int)p.groups;
+  const int64_t j0 = split * p.split_len;
+  const int64_t j1 = min(j0 + p.split_len, n);
+  const int nblocks = j0 < j1 ? (int)cdiv(j1 - j0, (int64_t)DK_BN) : 0;
+  dt_load_q<T>(p, kv * p.groups, rows, qs);
+  __syncthreads();
+  float m0 = -1.0e20f, m1 = -1.0e20f, l0 = 0.f, l1 = 0.f;
+  if (warp == DT_CONSUMERS) {
+    const T* K = static_cast<const T*>(p.k) + kv * p.sk_h;
+    int slot = 0;
+    uint32_t ph = 0;
+    for (int blk = 0; blk < nblocks; ++blk) {
+      if (blk >= DT_NST && !tc::mbar_wait_warp(smem_u32(c.empty + slot), ph ^ 1u, c.abort_flag, 46)) break;
+      const int64_t j = j0 + (int64_t)blk * DK_BN + lane;
+      dt_produce<T>(c.mask + slot, smem_u32(c.full + slot), j < j1 ? (int32_t)j : -1,
+                    j + 32 < j1 ? (int32_t)(j + 32) : -1, &maps.k, nullptr, kv * maps.k_head_rows, 0, K, p.sk_t,
+                    static_cast<const T*>(nullptr), 0, ring + (uint32_t)slot * DT_TILE, 0u);
+      if (++slot == DT_NST) {
+        slot = 0;
+        ph ^= 1u;
+      }
+    }
+  } else {
+    uint32_t qf[8][4];
+    dt_q_frags<T>(qs, qf);
+    const int key0 = warp * 16;
+    const int g = lane / 4, cc = 2 * (lane % 4);
+    const bool two = rows > 8;
+    float* srow0 = p.scores + (kv * p.groups + g) * p.cap;
+    float* srow1 = p.scores + (kv * p.groups + (two ? g + 8 : g)) * p.cap;
+    int slot = 0;
+    uint32_t ph = 0;
+    for (int b = 0; b < nblocks; ++b) {
+      if (!tc::mbar_wait_warp(smem_u32(c.full + slot), ph, c.abort_flag, 47)) break;
+      const uint64_t msk = c.mask[slot];
+      const int64_t jb = j0 + (int64_t)b * DK_BN;
+      float s[2][4];
+      dt_scores<T>(qf, ring + (uint32_t)slot * DT_TILE, key0, s);
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(smem_u32(c.empty + slot));
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int kk = key0 + t * 8 + cc;
+        const bool v0 = (msk >> kk) & 1u, v1 = (msk >> (kk + 1)) & 1u;
+        s[t][0] = v0 ? s[t][0] * p.scale_log2 : -INFINITY;
+        s[t][1] = v1 ? s[t][1] * p.scale_log2 : -INFINITY;
+        s[t][2] = v0 ? s[t][2] * p.scale_log2 : -INFINITY;
+        s[t][3] = v1 ? s[t][3] * p.scale_log2 : -INFINITY;
+        if (g < rows) {
+          if (v0) srow0[jb + kk] = s[t][0];
+          if (v1) srow0[jb + kk + 1] = s[t][1];
+        }
+        if (two && g + 8 < rows) {
+          if (v0) srow1[jb + kk] = s[t][2];
+          if (v1) srow1[jb + kk + 1] = s[t][3];
+        }
+        mx0 = fmaxf(mx0, fmaxf(s[t][0], s[t][1]));
+        mx1 = fmaxf(mx1, fmaxf(s[t][2], s[t][3]));
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      const float n0 = fmaxf(m0, mx0);
+      l0 = l0 * fast_exp2(m0 - n0) + (fast_exp2(s[0][0] - n0) + fast_exp2(s[0][1] - n0)) +
+           (fast_exp2(s[1][0] - n0) + fast_exp2(s[1][1] - n0));
+      m0 = n0;
+      if (two) {
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float n1 = fmaxf(m1, mx1);
+        l1 = l1 * fast_exp2(m1 - n1) + (fast_exp2(s[0][2] - n1) + fast_exp2(s[0][3] - n1)) +
+             (fast_exp2(s[1][2] - n1) + fast_exp2(s[1][3] - n1));
+        m1 = n1;
+      }
+      if (++slot == DT_NST) {
+        slot = 0;
+        ph ^= 1u;
+      }
+    }
+  }
+  __syncthreads();
+  if (*c.abort_flag) {
+    if (warp == DT_CONSUMERS && lane == 0)
+      for (int blk = max(0, nblocks - DT_NST); blk < nblocks; ++blk)
+        tc::mbar_drain(smem_u32(c.full + blk % DT_NST), (uint32_t)((blk / DT_NST) & 1));
+    return;
+  }
+  const uint32_t pad = ring - smem_u32(smem_raw);
+  float* wm = reinterpret_cast<float*>(smem_raw + pad);
+  float* wl = wm + DT_CONSUMERS * DK_MAXROWS;
+  if (warp < DT_CONSUMERS) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    const int g = lane / 4;
+    if (lane % 4 == 0) {
+      wm[warp * DK_MAXROWS + g] = m0;
+      wl[warp * DK_MAXROWS + g] = l0;
+      wm[warp * DK_MAXROWS + g + 8] = m1;
+      wl[warp * DK_MAXROWS + g + 8] = l1;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < rows) {
+    const int row = threadIdx.x;
+    float M = -1.0e20f;
+#pragma unroll
+    for (int w = 0; w < DT_CONSUMERS; ++w) M = fmaxf(M, wm[w * DK_MAXROWS + row]);
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < DT_CONSUMERS; ++w) L += wl[w * DK_MAXROWS + row] * fast_exp2(wm[w * DK_MAXROWS + row] - M);
+    const int64_t at = (kv * p.splits + split) * p.groups + row;
+    p.part_m[at] = M;
+    p.part_l[at] = L;
+  }
+}
+
 struct DecodePlan {
   int64_t splits, split_len;
   size_t m_bytes, l_bytes, acc_bytes, total;
@@ -579,6 +1049,34 @@ int64_t auto_splits(int64_t keys, int64_t ctas_per_split, size_t smem) {
   const int64_t per_sm = std::max<int64_t>(1, std::min<int64_t>(8, (int64_t)(233472 / (smem + 1024))));
   const int64_t wave = std::max<int64_t>(1, per_sm * num_sms() / ctas_per_split);
   return std::max<int64_t>(1, std::min<int64_t>({cdiv(keys, (int64_t)2 * DK_BN), wave, (int64_t)8192}));
+}
+
+// The TMA path: head_dim 128, fp16/bf16, each head's rows on one stride (s_t >= 128 elements)
+// and heads a whole number of rows apart, so that a 2-D [rows, 128] view covers the cache.
+bool dt_layout_ok(int64_t kv_heads, int64_t cap, int64_t s_h, int64_t s_t) {
+  if (s_t < 128 || (s_t * 2) % 16) return false;
+  if (kv_heads > 1 && (s_h <= 0 || s_h % s_t)) return false;
+  const int64_t head_rows = kv_heads > 1 ? s_h / s_t : 0;
+  return (kv_heads - 1) * head_rows + cap < ((int64_t)1 << 31);
+}
+bool dt_usable(const bb_decode_args* a, bool need_v) {
+  return a->d == 128 && (a->dtype == BB_BF16 || a->dtype == BB_F16) && tc::encode_fn() != nullptr &&
+         dt_layout_ok(a->kv_heads, a->cap, a->sk_h, a->sk_t) &&
+         (!need_v || dt_layout_ok(a->kv_heads, a->cap, a->sv_h, a->sv_t));
+}
+int dt_map(CUtensorMap* m, int64_t* head_rows, const void* base, int dtype, int64_t kv_heads, int64_t cap,
+           int64_t s_h, int64_t s_t) {
+  auto fn = tc::encode_fn();
+  *head_rows = kv_heads > 1 ? s_h / s_t : 0;
+  cuuint64_t dims[2] = {128, (cuuint64_t)((kv_heads - 1) * *head_rows + cap)};
+  cuuint64_t strides[1] = {(cuuint64_t)(s_t * 2)};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dtype == BB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(BB_ERR_LAUNCH, "decode: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return BB_OK;
 }
 
 int check_common(const bb_decode_args* a, int64_t rows_per_group_max) {
@@ -606,7 +1104,7 @@ int plan_decode(const bb_decode_args* a, DecodePlan* pl) {
   const int64_t rows = a->heads / rr;
   const int64_t total = a->front + a->window + a->route_k;
   int64_t splits = a->splits;
-  if (splits <= 0) splits = auto_splits(total, rr, dk_smem(dpad(a->d), true));
+  if (splits <= 0) splits = auto_splits(total, rr, dt_usable(a, true) ? DtSmem::bytes(true) : dk_smem(dpad(a->d), true));
   splits = std::min<int64_t>(splits, 8192);
   int64_t split_len = cdiv(cdiv(std::max<int64_t>(total, 1), splits), (int64_t)DK_BN) * DK_BN;
   splits = cdiv(std::max<int64_t>(total, 1), split_len);
@@ -657,10 +1155,21 @@ int launch_decode(const bb_decode_args* a, const DecodePlan& pl, char* ws, cudaS
   p.part_m = reinterpret_cast<float*>(ws);
   p.part_l = reinterpret_cast<float*>(ws + pl.m_bytes);
   p.part_acc = reinterpret_cast<float*>(ws + pl.m_bytes + pl.l_bytes);
-  const size_t smem = DkSmem<DP>::bytes(true);
-  cudaFuncSetAttribute(decode_partial_kernel<T, DP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  decode_partial_kernel<T, DP><<<dim3((unsigned)rr, (unsigned)pl.splits), DK_THREADS, smem, stream>>>(p);
-  BB_CHECK_LAUNCH("decode_partial_kernel");
+  if (DP == 128 && dt_usable(a, true)) {
+    DtMaps maps;
+    int st = dt_map(&maps.k, &maps.k_head_rows, a->k, a->dtype, a->kv_heads, a->cap, a->sk_h, a->sk_t);
+    if (!st) st = dt_map(&maps.v, &maps.v_head_rows, a->v, a->dtype, a->kv_heads, a->cap, a->sv_h, a->sv_t);
+    if (st) return st;
+    const size_t smem = DtSmem::bytes(true);
+    cudaFuncSetAttribute(decode_tma_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    decode_tma_kernel<T><<<dim3((unsigned)rr, (unsigned)pl.splits), DT_THREADS, smem, stream>>>(maps, p);
+    BB_CHECK_LAUNCH("decode_tma_kernel");
+  } else {
+    const size_t smem = DkSmem<DP>::bytes(true);
+    cudaFuncSetAttribute(decode_partial_kernel<T, DP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    decode_partial_kernel<T, DP><<<dim3((unsigned)rr, (unsigned)pl.splits), DK_THREADS, smem, stream>>>(p);
+    BB_CHECK_LAUNCH("decode_partial_kernel");
+  }
   decode_combine_kernel<T><<<(unsigned)a->heads, 128, (size_t)pl.splits * 4, stream>>>(p);
   BB_CHECK_LAUNCH("decode_combine_kernel");
   return BB_OK;
@@ -677,7 +1186,7 @@ int plan_droute(const bb_decode_args* a, DroutePlan* pl) {
   if (a->route_k < 0 || a->route_k > a->cap) return fail(BB_ERR_ARG, "decode_route: k_route must lie in [0, cap]");
   int64_t splits = a->splits;
   if (splits <= 0)
-    splits = auto_splits(a->cap, a->kv_heads, dk_smem(dpad(a->d), false));
+    splits = auto_splits(a->cap, a->kv_heads, dt_usable(a, false) ? DtSmem::bytes(false) : dk_smem(dpad(a->d), false));
   splits = std::min<int64_t>(splits, 8192);
   int64_t split_len = cdiv(cdiv(a->cap, splits), (int64_t)DK_BN) * DK_BN;
   splits = cdiv(a->cap, split_len);
@@ -701,10 +1210,21 @@ int launch_droute(const bb_decode_args* a, const DroutePlan& pl, char* ws, cudaS
   p.part_m = reinterpret_cast<float*>(ws + pl.scores_bytes);
   p.part_l = reinterpret_cast<float*>(ws + pl.scores_bytes + pl.m_bytes);
   p.probs = a->out_probs ? a->out_probs : reinterpret_cast<float*>(ws + pl.scores_bytes + pl.m_bytes + pl.l_bytes);
-  const size_t smem = DkSmem<DP>::bytes(false);
-  cudaFuncSetAttribute(droute_scores_kernel<T, DP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  droute_scores_kernel<T, DP><<<dim3((unsigned)a->kv_heads, (unsigned)pl.splits), DK_THREADS, smem, stream>>>(p);
-  BB_CHECK_LAUNCH("droute_scores_kernel");
+  if (DP == 128 && dt_usable(a, false)) {
+    DtMaps maps;
+    maps.v_head_rows = 0;
+    int st = dt_map(&maps.k, &maps.k_head_rows, a->k, a->dtype, a->kv_heads, a->cap, a->sk_h, a->sk_t);
+    if (st) return st;
+    const size_t smem = DtSmem::bytes(false);
+    cudaFuncSetAttribute(droute_tma_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    droute_tma_kernel<T><<<dim3((unsigned)a->kv_heads, (unsigned)pl.splits), DT_THREADS, smem, stream>>>(maps, p);
+    BB_CHECK_LAUNCH("droute_tma_kernel");
+  } else {
+    const size_t smem = DkSmem<DP>::bytes(false);
+    cudaFuncSetAttribute(droute_scores_kernel<T, DP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    droute_scores_kernel<T, DP><<<dim3((unsigned)a->kv_heads, (unsigned)pl.splits), DK_THREADS, smem, stream>>>(p);
+    BB_CHECK_LAUNCH("droute_scores_kernel");
+  }
   droute_pool_kernel<<<dim3((unsigned)a->kv_heads, (unsigned)cdiv(a->cap, (int64_t)1024)), 256, 0, stream>>>(p);
   BB_CHECK_LAUNCH("droute_pool_kernel");
   if (a->route_k > 0 && a->out_idx) {
