@@ -256,3 +256,16 @@ def test_fused_rmsnorm_model_close_to_hf():
     a, b = got[0][0], want[0][0]
     assert (a - b).abs().max() < 0.1
     assert (a.argmax(-1) == b.argmax(-1)).float().mean() > 0.97
+
+
+def test_native_chunked_mlp_batch_two():
+    """Leading batch dim: chunks are strided slices of the input and of the output (37 tokens, not
+    a multiple of the chunk), still equal to HF's MLP on the same chunks."""
+    model = tiny(1)
+    mlp = model.model.layers[0].mlp
+    x = torch.randn(2, 37, 256, device=DEV, dtype=torch.bfloat16)
+    with torch.inference_mode():
+        want = torch.cat([mlp(x[:, s:s + 8]) for s in range(0, 37, 8)], dim=1)
+        install_chunked_mlp(model, 8)
+        got = mlp(x)
+    assert torch.equal(got, want)

@@ -81,6 +81,10 @@ def test_memory_entry_points_check_arguments():
     assert L.bb_embed_gather(p, 10, 24, p, 1, p, p, None) != 0                         # row not 16-byte multiple
     assert L.bb_embed_gather(p, 0, 16, p, 1, p, p, None) != 0                          # empty vocab
     assert L.bb_embed_gather(p, 10, 16, p, 0, p, p, None) == 0                         # no ids
+    assert L.bb_rmsnorm(p, 8, None, 0, p, p, 8, 0, 8, 1e-5, _lib.BB_BF16, None) == 0   # no rows
+    assert L.bb_rmsnorm(None, 8, None, 0, p, p, 8, 2, 8, 1e-5, _lib.BB_BF16, None) != 0  # null x
+    assert L.bb_rmsnorm(p, 12, None, 0, p, p, 12, 2, 12, 1e-5, _lib.BB_BF16, None) != 0  # rows not 16-byte multiples
+    assert L.bb_rmsnorm(p, 8, None, 0, p, p, 8, 2, 8, 1e-5, 9, None) != 0              # bad dtype
 
 
 def test_python_memory_ops_reject_cpu_tensors():
