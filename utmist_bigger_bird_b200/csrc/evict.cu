@@ -4,7 +4,8 @@
 //                            heads (the scatter of :240-241 reduced over the group, :247).
 //   2. evict_score_kernel    score[kv, j] = max over the group's query heads of col[h, j] (:243).
 //   3. evict_prio_kernel     prio = 2 * member + forward_pool(score) (:245-247, :70-75), with the
-//                            sink keys and the last `window` keys at -inf (:249-250).
+//                            sink keys and the last `window` keys at -inf (:249-250). Without a
+//                            forward pool, steps 2-3 run as one pass (evict_prio_direct_kernel).
 //   4. route_topk_kernel     the `keep` largest priorities per KV head, positions ascending
 //                            (:252, shared with routing).
 //   5. evict_gather_kernel   kept positions [sink | selected | window] and the K/V rows at them,
@@ -65,6 +66,21 @@ __global__ void evict_prio_kernel(EvictParams p) {
     } else {
       s = sc[j];
     }
+    pr = (p.member[t] ? 2.f : 0.f) + s;
+  }
+  p.prio[t] = pr;
+}
+
+// Steps 2-3 in one pass when there is no forward pool (the default policy): the group max of the
+// column scores goes straight into the priority.
+__global__ void evict_prio_direct_kernel(EvictParams p) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= p.kv_heads * p.n) return;
+  const int64_t kv = t / p.n, j = t % p.n;
+  float pr = -INFINITY;
+  if (j >= p.sink && j < p.n - p.window) {
+    float s = -INFINITY;
+    for (int64_t g = 0; g < p.groups; ++g) s = fmaxf(s, p.col[(kv * p.groups + g) * p.sc_h + j]);
     pr = (p.member[t] ? 2.f : 0.f) + s;
   }
   p.prio[t] = pr;
@@ -166,10 +182,15 @@ int kv_evict(const bb_evict_args* a, void* ws, size_t ws_bytes, cudaStream_t str
     evict_member_kernel<<<(unsigned)cdiv(a->heads * a->budget, (int64_t)256), 256, 0, stream>>>(p);
     BB_CHECK_LAUNCH("evict_member_kernel");
   }
-  evict_score_kernel<<<(unsigned)cdiv(cells, (int64_t)256), 256, 0, stream>>>(p);
-  BB_CHECK_LAUNCH("evict_score_kernel");
-  evict_prio_kernel<<<(unsigned)cdiv(cells, (int64_t)256), 256, 0, stream>>>(p);
-  BB_CHECK_LAUNCH("evict_prio_kernel");
+  if (p.pool > 1 || p.pool_back > 0) {
+    evict_score_kernel<<<(unsigned)cdiv(cells, (int64_t)256), 256, 0, stream>>>(p);
+    BB_CHECK_LAUNCH("evict_score_kernel");
+    evict_prio_kernel<<<(unsigned)cdiv(cells, (int64_t)256), 256, 0, stream>>>(p);
+    BB_CHECK_LAUNCH("evict_prio_kernel");
+  } else {
+    evict_prio_direct_kernel<<<(unsigned)cdiv(cells, (int64_t)256), 256, 0, stream>>>(p);
+    BB_CHECK_LAUNCH("evict_prio_direct_kernel");
+  }
   if (a->keep > 0) {
     st = topk_sorted(p.prio, a->kv_heads, a->n, a->keep, p.sel, a->keep, stream);
     if (st) return st;

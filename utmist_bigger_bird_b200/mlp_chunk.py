@@ -56,7 +56,11 @@ def _swiglu_chunked(mlp, chunk: int, base):
             torch.matmul(xs, wg.t(), out=g)
             torch.matmul(xs, wu.t(), out=u)
             _ops.silu_mul_(g, u)
-            torch.matmul(g, wd.t(), out=out[..., s:e, :])
+            dst = out[..., s:e, :]
+            if dst.is_contiguous():  # batch 1: straight into the output rows
+                torch.matmul(g, wd.t(), out=dst)
+            else:
+                dst.copy_(torch.matmul(g, wd.t()))
         reduce = getattr(_mlp.down_proj, "all_reduce_", None)  # tensor-parallel down projection
         return reduce(out) if reduce is not None else out
 
