@@ -126,3 +126,16 @@ def test_decode_errors():
         bigger_bird_decode(q, k, v, idx, front=64, window=4096)       # cache shorter than front + window
     with pytest.raises(ValueError):
         pooled_probs(q.float(), k)
+
+
+@pytest.mark.parametrize("splits", [1, 7, 5000])
+def test_decode_explicit_splits(splits):
+    """Caller-chosen split counts (one split, an odd count, more than the cap of 4096) give the
+    same output as the oracle."""
+    from utmist_bigger_bird_b200 import bigger_bird_decode
+    H, hk, cap, d, front, window, R = 32, 8, 16384, 128, 64, 4096, 256
+    q, k, v = make(H, hk, cap, d)
+    idx = routes(hk, R, front, cap - window)
+    out = bigger_bird_decode(q, k, v, idx, front=front, window=window, scale=d ** -0.5, splits=splits)
+    want = orc.decode(np32(q), np32(k), np32(v), idx.cpu().numpy(), front=front, window=window, scale=d ** -0.5)
+    close(out, want, f"splits={splits}")

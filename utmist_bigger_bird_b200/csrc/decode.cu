@@ -341,17 +341,21 @@ __global__ void __launch_bounds__(DK_THREADS, 2) decode_partial_kernel(DecodePar
 // One CTA per query head merges its splits: w_s = exp2(m_s - max m), out = sum w_s acc_s / sum w_s l_s.
 template <typename T>
 __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeParams p) {
-  extern __shared__ float wsm[];  // [splits]
+  extern __shared__ float wsm[];  // [splits] weights, then [splits] l
   __shared__ float red[4];
+  __shared__ float4 part[4][32];   // per warp: its splits' share of the 128 columns
   const int64_t h = blockIdx.x;
   const int64_t r = h / p.rows, row = h % p.rows;
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
   const int S = (int)p.splits;
+  float* lsm = wsm + S;
   auto at = [&](int s) { return (r * p.splits + s) * p.rows + row; };
+  // m and l of every split in one round of loads
   float M = -INFINITY;
   for (int s = threadIdx.x; s < S; s += 128) {
     const float m = p.part_m[at(s)];
     wsm[s] = m;
+    lsm[s] = p.part_l[at(s)];
     M = fmaxf(M, m);
   }
 #pragma unroll
@@ -363,7 +367,7 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeParams p) {
   for (int s = threadIdx.x; s < S; s += 128) {
     const float w = fast_exp2(wsm[s] - M);
     wsm[s] = w;
-    L += p.part_l[at(s)] * w;
+    L += lsm[s] * w;
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
@@ -371,18 +375,29 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeParams p) {
   if (lane == 0) red[warp] = L;
   __syncthreads();
   L = (red[0] + red[1]) + (red[2] + red[3]);
-  T* o = static_cast<T*>(p.out) + h * p.so_h;
-  for (int64_t col = threadIdx.x; col < p.d; col += 128) {
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    int s = 0;
-    for (; s + 4 <= S; s += 4) {
-      a0 += p.part_acc[at(s) * p.d + col] * wsm[s];
-      a1 += p.part_acc[at(s + 1) * p.d + col] * wsm[s + 1];
-      a2 += p.part_acc[at(s + 2) * p.d + col] * wsm[s + 2];
-      a3 += p.part_acc[at(s + 3) * p.d + col] * wsm[s + 3];
+  // Warp w sums splits w, w + 4, ...; lane holds 4 columns (16-byte loads, independent of each other).
+  const bool live = 4 * lane < p.d;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (live) {
+#pragma unroll 4
+    for (int sp = warp; sp < S; sp += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(p.part_acc + at(sp) * p.d + 4 * lane);
+      const float wv = wsm[sp];
+      acc.x += v.x * wv;
+      acc.y += v.y * wv;
+      acc.z += v.z * wv;
+      acc.w += v.w * wv;
     }
-    for (; s < S; ++s) a0 += p.part_acc[at(s) * p.d + col] * wsm[s];
-    o[col] = Elem<T>::from_f(((a0 + a1) + (a2 + a3)) / L);
+  }
+  part[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && live) {
+    const float4 a0 = part[0][lane], a1 = part[1][lane], a2 = part[2][lane], a3 = part[3][lane];
+    T* o = static_cast<T*>(p.out) + h * p.so_h + 4 * lane;
+    o[0] = Elem<T>::from_f(((a0.x + a1.x) + (a2.x + a3.x)) / L);
+    o[1] = Elem<T>::from_f(((a0.y + a1.y) + (a2.y + a3.y)) / L);
+    o[2] = Elem<T>::from_f(((a0.z + a1.z) + (a2.z + a3.z)) / L);
+    o[3] = Elem<T>::from_f(((a0.w + a1.w) + (a2.w + a3.w)) / L);
   }
 }
 
@@ -1105,7 +1120,7 @@ int plan_decode(const bb_decode_args* a, DecodePlan* pl) {
   const int64_t total = a->front + a->window + a->route_k;
   int64_t splits = a->splits;
   if (splits <= 0) splits = auto_splits(total, rr, dt_usable(a, true) ? DtSmem::bytes(true) : dk_smem(dpad(a->d), true));
-  splits = std::min<int64_t>(splits, 8192);
+  splits = std::min<int64_t>(splits, 4096);  // the combine keeps two floats a split in shared memory (32 KB)
   int64_t split_len = cdiv(cdiv(std::max<int64_t>(total, 1), splits), (int64_t)DK_BN) * DK_BN;
   splits = cdiv(std::max<int64_t>(total, 1), split_len);
   pl->splits = splits;
@@ -1170,7 +1185,7 @@ int launch_decode(const bb_decode_args* a, const DecodePlan& pl, char* ws, cudaS
     decode_partial_kernel<T, DP><<<dim3((unsigned)rr, (unsigned)pl.splits), DK_THREADS, smem, stream>>>(p);
     BB_CHECK_LAUNCH("decode_partial_kernel");
   }
-  decode_combine_kernel<T><<<(unsigned)a->heads, 128, (size_t)pl.splits * 4, stream>>>(p);
+  decode_combine_kernel<T><<<(unsigned)a->heads, 128, (size_t)pl.splits * 8, stream>>>(p);
   BB_CHECK_LAUNCH("decode_combine_kernel");
   return BB_OK;
 }
