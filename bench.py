@@ -260,6 +260,7 @@ def side_paths(cfg, qr, kr, v, idx, qpos, budget, dev, stream, reps, pk, parts=(
     g = H // per
     scrub = torch.ones(64 << 20, device=dev, dtype=torch.float32)  # 256 MB, twice L2
     evict_line = decode_line = None
+    w = min(cfg.window, n - cfg.sink)  # the window the module uses when it covers the whole prompt
     if "evict" in parts:
         # ---- KV eviction after the prefill (RDAttention.evict, default policy): priorities from the
         # step's routes and routing column scores, the g*budget best middle keys, K/V gather. HBM-bound;
@@ -268,15 +269,15 @@ def side_paths(cfg, qr, kr, v, idx, qpos, budget, dev, stream, reps, pk, parts=(
         col_buf = torch.empty(H, n, device=dev, dtype=torch.float32)
         _ops.routes_(qr[0], kr[0], qpos, sink=cfg.sink, window=cfg.window, budget=budget, scaling=cfg.scaling,
                      out_col=col_buf)
-        keep = min(g * budget, n - cfg.sink - cfg.window)
+        keep = min(g * budget, n - cfg.sink - w)
 
         def evict():
-            _ops.kv_evict_(idx, col_buf, kr[0], v[0], sink=cfg.sink, window=cfg.window, keep=keep)
+            _ops.kv_evict_(idx, col_buf, kr[0], v[0], sink=cfg.sink, window=w, keep=keep)
 
         evict()
         torch.cuda.synchronize(dev)
         evict_ms = flushed_time(evict, reps, stream, scrub)
-        kept_rows = cfg.sink + keep + cfg.window
+        kept_rows = cfg.sink + keep + w
         evict_bytes = H * n * 4 + 2 * 2 * per * kept_rows * d * 2
         evict_gbs = evict_bytes / (evict_ms * 1e-3) / 1e9
         evict_line = {"bound": "hbm", "ms": evict_ms, "kept_rows_per_kv_head": kept_rows, "achieved_gbs": evict_gbs,
@@ -289,12 +290,12 @@ def side_paths(cfg, qr, kr, v, idx, qpos, budget, dev, stream, reps, pk, parts=(
         # K (and V) rows each one must read.
         from utmist_bigger_bird_b200 import bigger_bird_decode, bigger_bird_route
         qd = qr[0, :, n - 1].contiguous()
-        droute = lambda: bigger_bird_route(qd, kr[0], budget, front=cfg.sink, window=cfg.window,  # noqa: E731
+        droute = lambda: bigger_bird_route(qd, kr[0], budget, front=cfg.sink, window=w,  # noqa: E731
                                            scale=cfg.scaling)
-        didx = droute()
-        dsparse = lambda: bigger_bird_decode(qd, kr[0], v[0], didx, front=cfg.sink, window=cfg.window,  # noqa: E731
+        no_routes = torch.empty(per, 0, dtype=torch.int64, device=dev)
+        didx = droute() if budget > 0 else no_routes
+        dsparse = lambda: bigger_bird_decode(qd, kr[0], v[0], didx, front=cfg.sink, window=w,  # noqa: E731
                                              scale=cfg.scaling)
-        no_routes = didx[:, :0]
         ddense = lambda: bigger_bird_decode(qd, kr[0], v[0], no_routes, front=0, window=n,  # noqa: E731
                                             scale=cfg.scaling)
         for fn in (dsparse, ddense):
@@ -302,14 +303,16 @@ def side_paths(cfg, qr, kr, v, idx, qpos, budget, dev, stream, reps, pk, parts=(
         torch.cuda.synchronize(dev)
         dec = {}
         for name, fn, nbytes in (("route", droute, per * n * d * 2),
-                                 ("sparse", dsparse, 2 * per * (cfg.sink + cfg.window + budget) * d * 2),
+                                 ("sparse", dsparse, 2 * per * (cfg.sink + w + budget) * d * 2),
                                  ("dense", ddense, 2 * per * n * d * 2)):
+            if name == "route" and budget == 0:
+                continue  # nothing to route: front and window cover the cache
             t = flushed_time(fn, reps * 3, stream, scrub)
             gbs = nbytes / (t * 1e-3) / 1e9
             dec[name] = {"ms": t, "algorithmic_bytes": nbytes, "achieved_gbs": gbs, "frac": gbs / pk["hbm_gbs"]}
         decode_line = dict(dec, bound="hbm", peak_gbs=pk["hbm_gbs"],
                            config=f"one token per head over the rank's {n}-key cache: route = pooled probabilities + "
-                                  f"top-{budget} per KV head; sparse = front {cfg.sink} | window {cfg.window} | "
+                                  f"top-{budget} per KV head; sparse = front {cfg.sink} | window {w} | "
                                   f"{budget} pooled routes; dense = all keys")
     return evict_line, decode_line
 
