@@ -55,7 +55,7 @@ typedef enum { BB_POOL_MEAN = 0, BB_POOL_MAX = 1 } bb_pool;
 BB_API const char* bb_last_error(void);
 /* Library ABI version (BB_ABI_VERSION). */
 BB_API int bb_abi_version(void);
-#define BB_ABI_VERSION 1
+#define BB_ABI_VERSION 2
 /* Number of CUDA kernels this library has launched in this process (all threads, all devices).
  * Instrumentation for benchmarks; no counterpart in the reference. */
 BB_API uint64_t bb_kernel_launches(void);
@@ -228,7 +228,7 @@ typedef struct {
   const void* q; int64_t sq_h;              /* [H, d], innermost stride 1 */
   const void* k; int64_t sk_h, sk_t;        /* [Hkv, cap, d] */
   const void* v; int64_t sv_h, sv_t;        /* [Hkv, cap, d] (bb_decode only) */
-  const int32_t* idx; int64_t si_r;         /* [route_rows, route_k] (bb_decode) */
+  const void* idx; int64_t si_r;            /* [route_rows, route_k] int32, or int64 when idx_i64 (bb_decode) */
   int64_t route_rows, route_k;              /* bb_decode_route: route_k = keys to select */
   int64_t n; const int64_t* n_dev;          /* valid keys: n, or *n_dev when n_dev != NULL */
   int64_t cap, heads, kv_heads, d;
@@ -239,6 +239,8 @@ typedef struct {
   float* out_probs;                         /* bb_decode_route: [Hkv, cap] or NULL */
   int32_t* out_idx; int64_t so_i;           /* bb_decode_route: [Hkv, route_k] or NULL */
   int dtype;                                /* BB_F16 / BB_BF16 */
+  int idx_i64;                              /* bb_decode: 1 when idx holds int64 positions (the
+                                              routes' torch dtype, read as is: no conversion pass) */
 } bb_decode_args;
 
 BB_API int bb_decode_workspace_size(const bb_decode_args* a, size_t* bytes);

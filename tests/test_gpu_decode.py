@@ -139,3 +139,23 @@ def test_decode_explicit_splits(splits):
     out = bigger_bird_decode(q, k, v, idx, front=front, window=window, scale=d ** -0.5, splits=splits)
     want = orc.decode(np32(q), np32(k), np32(v), idx.cpu().numpy(), front=front, window=window, scale=d ** -0.5)
     close(out, want, f"splits={splits}")
+
+
+@pytest.mark.parametrize("d", [128, 64])
+def test_decode_route_index_dtypes(d):
+    """Routes as int64 (the dtype bigger_bird_route returns) and as int32 are read as given (no
+    conversion pass): the outputs are bit-identical."""
+    from utmist_bigger_bird_b200 import bigger_bird_decode
+    H, hk, cap, front, window, R = 32, 8, 16384, 64, 4096, 300
+    q, k, v = make(H, hk, cap, d)
+    idx = routes(hk, R, front, cap - window)
+    assert idx.dtype == torch.int64
+    kw = dict(front=front, window=window, scale=d ** -0.5)
+    o64 = bigger_bird_decode(q, k, v, idx, **kw)
+    o32 = bigger_bird_decode(q, k, v, idx.to(torch.int32), **kw)
+    assert torch.equal(o64, o32)
+    # a strided int64 view (every other column of a wider tensor) is made contiguous first
+    wide = torch.stack([idx, idx], -1).reshape(hk, 2 * R)[:, ::2]
+    assert torch.equal(bigger_bird_decode(q, k, v, wide, **kw), o64)
+    want = orc.decode(np32(q), np32(k), np32(v), idx.cpu().numpy(), **kw)
+    close(o64, want, f"int64 routes d={d}")

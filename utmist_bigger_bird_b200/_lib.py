@@ -13,7 +13,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libbb_b200.so"
 
 BB_F16, BB_BF16, BB_F32 = 0, 1, 2
 BB_POOL_MEAN, BB_POOL_MAX = 0, 1
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _VALUE_ERRORS = {1, 2, 3, 4, 5, 7}
 _STATUS = {0: "BB_OK", 1: "BB_ERR_ARG", 2: "BB_ERR_SHAPE", 3: "BB_ERR_DTYPE", 4: "BB_ERR_STRIDE",
@@ -88,7 +88,7 @@ class DecodeArgs(C.Structure):
                 ("out", vp), ("so_h", i64),
                 ("out_probs", vp),
                 ("out_idx", vp), ("so_i", i64),
-                ("dtype", C.c_int)]
+                ("dtype", C.c_int), ("idx_i64", C.c_int)]
 
 
 EXPORTS = {

@@ -194,7 +194,7 @@ def _n_arg(n, cap, device):
 
 def decode_(q, k, v, idx, out, *, front, window, scale, n=None, splits=0):
     """One-token sparse decode: q [H, d], k/v [Hkv, cap, d] (cache views), idx [Hkv or H, R] int32
-    (or None), out [H, d]. ``n``: cache length (None = cap, int, or 1-element GPU tensor)."""
+    or int64 (or None), out [H, d]. ``n``: cache length (None = cap, int, or 1-element GPU tensor)."""
     H, d = q.shape
     hk, cap, _ = k.shape
     if k.stride(-1) != 1 or v.stride(-1) != 1 or q.stride(-1) != 1 or out.stride(-1) != 1:
@@ -207,7 +207,7 @@ def decode_(q, k, v, idx, out, *, front, window, scale, n=None, splits=0):
                         route_rows=idx.shape[0] if idx is not None else hk, route_k=R,
                         n=n_host, n_dev=n_ptr, cap=cap, heads=H, kv_heads=hk, d=d, front=front, window=window,
                         scale=scale, splits=splits or 0, out=out.data_ptr(), so_h=out.stride(0),
-                        dtype=_DT[q.dtype])
+                        dtype=_DT[q.dtype], idx_i64=int(R > 0 and idx.dtype == torch.int64))
     L = _lib.lib()
     nbytes = C.c_size_t(0)
     _lib.check(L.bb_decode_workspace_size(C.byref(a), C.byref(nbytes)), "bigger_bird_decode")

@@ -40,7 +40,8 @@ def bigger_bird_decode(q, k, v, indices, *, front=64, window=4096, scale=1.0, n=
         raise ValueError("indices must be [Hkv, R] (pooled) or [H, R] (per head)")
     if k.dtype != q.dtype or v.dtype != q.dtype:
         raise ValueError("q, k and v must share one dtype")
-    idx = indices.to(torch.int32) if indices.dtype != torch.int32 else indices
+    # int32 and int64 (the routes' dtype) are read as they are; other integer dtypes are widened.
+    idx = indices if indices.dtype in (torch.int32, torch.int64) else indices.to(torch.int64)
     if idx.numel() and idx.stride(-1) != 1:
         idx = idx.contiguous()
     q = q if q.stride(-1) == 1 else q.contiguous()

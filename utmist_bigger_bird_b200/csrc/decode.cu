@@ -44,7 +44,8 @@ struct DecodeParams {
   const void* q; int64_t sq_h;
   const void* k; int64_t sk_h, sk_t;
   const void* v; int64_t sv_h, sv_t;
-  const int32_t* idx; int64_t si_r;  // [route rows][route_k]
+  const void* idx; int64_t si_r;  // [route rows][route_k], int32 or (idx64) int64
+  int idx64;
   const int64_t* n_dev;
   int64_t n, cap, d, heads, kv_heads, groups, rows, route_rows, route_k, front, window;
   int64_t splits, split_len;
@@ -84,7 +85,10 @@ __device__ __forceinline__ int64_t virtual_pos(const DecodeParams& p, int64_t r,
   int64_t pos;
   if (j < p.front) pos = j;
   else if (j < p.front + p.window) pos = n - p.window + (j - p.front);
-  else pos = p.idx[r * p.si_r + (j - p.front - p.window)];
+  else {
+    const int64_t o = r * p.si_r + (j - p.front - p.window);
+    pos = p.idx64 ? static_cast<const int64_t*>(p.idx)[o] : (int64_t) static_cast<const int32_t*>(p.idx)[o];
+  }
   return (pos >= 0 && pos < n) ? pos : -1;
 }
 
@@ -1148,7 +1152,7 @@ DecodeParams make_params(const bb_decode_args* a) {
   p.q = a->q; p.sq_h = a->sq_h;
   p.k = a->k; p.sk_h = a->sk_h; p.sk_t = a->sk_t;
   p.v = a->v; p.sv_h = a->sv_h; p.sv_t = a->sv_t;
-  p.idx = a->idx; p.si_r = a->si_r;
+  p.idx = a->idx; p.si_r = a->si_r; p.idx64 = a->idx_i64 != 0;
   p.n_dev = a->n_dev;
   p.n = a->n; p.cap = a->cap; p.d = a->d; p.heads = a->heads; p.kv_heads = a->kv_heads;
   p.groups = a->heads / a->kv_heads;
