@@ -221,8 +221,8 @@ BB_API int bb_kv_evict(const bb_evict_args* a, void* workspace, size_t workspace
  * bb_decode_route (pooled_probs / bigger_bird_route, kernels/bigger_bird_route.py:80-115): per KV
  * head, the probability of every cached key under each query head's softmax over the first n
  * keys, averaged over the KV head's query heads; -1 outside [front, n - window). out_probs (may be
- * NULL): [Hkv, cap] fp32; out_idx (may be NULL): [Hkv, route_k] int32, the route_k most probable
- * keys, positions ascending.
+ * NULL): [Hkv, cap] fp32; out_idx (may be NULL): [Hkv, route_k] int32 (int64 with out_idx_i64),
+ * the route_k most probable keys, positions ascending.
  */
 typedef struct {
   const void* q; int64_t sq_h;              /* [H, d], innermost stride 1 */
@@ -237,10 +237,12 @@ typedef struct {
   int64_t splits;                           /* 0: enough chunks for ~4 CTAs per SM */
   void* out; int64_t so_h;                  /* bb_decode: [H, d] */
   float* out_probs;                         /* bb_decode_route: [Hkv, cap] or NULL */
-  int32_t* out_idx; int64_t so_i;           /* bb_decode_route: [Hkv, route_k] or NULL */
+  void* out_idx; int64_t so_i;              /* bb_decode_route: [Hkv, route_k] int32 (int64 when
+                                              out_idx_i64) or NULL */
   int dtype;                                /* BB_F16 / BB_BF16 */
   int idx_i64;                              /* bb_decode: 1 when idx holds int64 positions (the
                                               routes' torch dtype, read as is: no conversion pass) */
+  int out_idx_i64;                          /* bb_decode_route: 1 to write out_idx as int64 */
 } bb_decode_args;
 
 BB_API int bb_decode_workspace_size(const bb_decode_args* a, size_t* bytes);

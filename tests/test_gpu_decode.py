@@ -159,3 +159,17 @@ def test_decode_route_index_dtypes(d):
     assert torch.equal(bigger_bird_decode(q, k, v, wide, **kw), o64)
     want = orc.decode(np32(q), np32(k), np32(v), idx.cpu().numpy(), **kw)
     close(o64, want, f"int64 routes d={d}")
+
+
+def test_decode_route_output_widths():
+    """bigger_bird_route's int64 routes (written as int64 by the top-k) equal the int32 output of
+    the same call, and both are the reference's dtype-independent position sets."""
+    from utmist_bigger_bird_b200 import _ops, bigger_bird_route
+    H, hk, cap, d, front, window, R = 32, 8, 16384, 128, 64, 4096, 300
+    q, k, _ = make(H, hk, cap, d)
+    i64 = bigger_bird_route(q, k, R, front=front, window=window, scale=d ** -0.5)
+    assert i64.dtype == torch.int64 and i64.shape == (hk, R)
+    i32 = torch.empty(hk, R, dtype=torch.int32, device=DEV)
+    _ops.decode_route_(q, k, front=front, window=window, scale=d ** -0.5, k_route=R, idx_out=i32)
+    assert torch.equal(i64, i32.long())
+    assert bool((i64[:, 1:] > i64[:, :-1]).all())

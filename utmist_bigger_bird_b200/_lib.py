@@ -88,7 +88,7 @@ class DecodeArgs(C.Structure):
                 ("out", vp), ("so_h", i64),
                 ("out_probs", vp),
                 ("out_idx", vp), ("so_i", i64),
-                ("dtype", C.c_int), ("idx_i64", C.c_int)]
+                ("dtype", C.c_int), ("idx_i64", C.c_int), ("out_idx_i64", C.c_int)]
 
 
 EXPORTS = {

@@ -219,7 +219,7 @@ def decode_(q, k, v, idx, out, *, front, window, scale, n=None, splits=0):
 
 def decode_route_(q, k, *, front, window, scale, n=None, k_route=0, probs=None, idx_out=None, splits=0):
     """Decode routing: pooled probabilities [Hkv, cap] fp32 into ``probs`` (optional) and the
-    ``k_route`` most probable keys per KV head into ``idx_out`` [Hkv, k_route] int32 (optional)."""
+    ``k_route`` most probable keys per KV head into ``idx_out`` [Hkv, k_route] int32 or int64 (optional)."""
     H, d = q.shape
     hk, cap, _ = k.shape
     if k.stride(-1) != 1 or q.stride(-1) != 1:
@@ -230,7 +230,8 @@ def decode_route_(q, k, *, front, window, scale, n=None, k_route=0, probs=None, 
                         d=d, front=front, window=window, scale=scale, splits=splits or 0,
                         out_probs=probs.data_ptr() if probs is not None else None,
                         out_idx=idx_out.data_ptr() if idx_out is not None else None,
-                        so_i=idx_out.stride(0) if idx_out is not None else 0, dtype=_DT[q.dtype])
+                        so_i=idx_out.stride(0) if idx_out is not None else 0, dtype=_DT[q.dtype],
+                        out_idx_i64=int(idx_out is not None and idx_out.dtype == torch.int64))
     L = _lib.lib()
     nbytes = C.c_size_t(0)
     _lib.check(L.bb_decode_route_workspace_size(C.byref(a), C.byref(nbytes)), "bigger_bird_route")

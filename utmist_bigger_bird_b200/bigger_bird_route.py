@@ -48,7 +48,7 @@ def bigger_bird_route(q, k, k_route, *, front=64, window=4096, scale=1.0, n=None
     hk, cap, _ = k.shape
     if not 0 <= k_route <= cap:
         raise ValueError("k_route must lie in [0, capacity]")
-    idx = torch.empty(hk, k_route, device=q.device, dtype=torch.int32)
+    idx = torch.empty(hk, k_route, device=q.device, dtype=torch.int64)  # written as int64 by the top-k
     _ops.decode_route_(q, k, front=front, window=window, scale=scale, n=n, k_route=k_route, idx_out=idx,
                        splits=kw.get("splits") or 0)
-    return idx.long()
+    return idx

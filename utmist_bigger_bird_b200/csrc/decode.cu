@@ -28,7 +28,7 @@
 
 namespace bb {
 
-int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, int32_t* out, int64_t so_h,
+int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, void* out, bool out64, int64_t so_h,
                 cudaStream_t stream);
 
 namespace {
@@ -1247,7 +1247,7 @@ int launch_droute(const bb_decode_args* a, const DroutePlan& pl, char* ws, cudaS
   droute_pool_kernel<<<dim3((unsigned)a->kv_heads, (unsigned)cdiv(a->cap, (int64_t)1024)), 256, 0, stream>>>(p);
   BB_CHECK_LAUNCH("droute_pool_kernel");
   if (a->route_k > 0 && a->out_idx) {
-    int st = topk_sorted(p.probs, a->kv_heads, a->cap, a->route_k, a->out_idx, a->so_i, stream);
+    int st = topk_sorted(p.probs, a->kv_heads, a->cap, a->route_k, a->out_idx, a->out_idx_i64 != 0, a->so_i, stream);
     if (st) return st;
   }
   return BB_OK;

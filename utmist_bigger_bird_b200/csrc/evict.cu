@@ -18,7 +18,7 @@
 
 namespace bb {
 
-int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, int32_t* out, int64_t so_h,
+int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, void* out, bool out64, int64_t so_h,
                 cudaStream_t stream);
 
 namespace {
@@ -192,7 +192,7 @@ int kv_evict(const bb_evict_args* a, void* ws, size_t ws_bytes, cudaStream_t str
     BB_CHECK_LAUNCH("evict_prio_direct_kernel");
   }
   if (a->keep > 0) {
-    st = topk_sorted(p.prio, a->kv_heads, a->n, a->keep, p.sel, a->keep, stream);
+    st = topk_sorted(p.prio, a->kv_heads, a->n, a->keep, p.sel, false, a->keep, stream);
     if (st) return st;
   }
   const int64_t L = a->sink + a->keep + a->window;

@@ -23,7 +23,7 @@
 
 namespace bb {
 
-int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, int32_t* out, int64_t so_h,
+int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, void* out, bool out64, int64_t so_h,
                 cudaStream_t stream);
 namespace {
 
@@ -414,9 +414,10 @@ __device__ __forceinline__ unsigned lowest_bits(unsigned m, int k) {
 
 // One CTA per query head. Each thread owns 16 consecutive scores of a 16K-score chunk (vector
 // loads, 16x fewer dependent iterations than one score per thread).
+template <typename OutT>
 __global__ void __launch_bounds__(TK_THREADS) route_topk_kernel(const float* __restrict__ col,
                                                                 int64_t n, int64_t budget,
-                                                                int32_t* __restrict__ out,
+                                                                OutT* __restrict__ out,
                                                                 int64_t so_h) {
   __shared__ unsigned int hist[256];
   __shared__ int warp_sums[32];
@@ -424,7 +425,7 @@ __global__ void __launch_bounds__(TK_THREADS) route_topk_kernel(const float* __r
   __shared__ int64_t sel_rem;
   const int64_t h = blockIdx.x;
   const float* c = col + h * n;
-  int32_t* o = out + h * so_h;
+  OutT* o = out + h * so_h;
   if (budget <= 0) return;
   const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(c) & 15) == 0);
   constexpr int64_t CHUNK = (int64_t)TK_THREADS * TK_VEC;
@@ -503,7 +504,7 @@ __global__ void __launch_bounds__(TK_THREADS) route_topk_kernel(const float* __r
 #pragma unroll
     for (int e = 0; e < TK_VEC; ++e) {
       if ((takem >> e) & 1u) {
-        if (pos < budget) o[pos] = (int32_t)(i0 + e);
+        if (pos < budget) o[pos] = (OutT)(i0 + e);
         ++pos;
       }
     }
@@ -596,7 +597,7 @@ int launch_routes_t(const bb_routes_args* a, const RtPlan& pl, char* ws, cudaStr
     route_col_kernel<T, DP><<<grid, RT_THREADS, smem, stream>>>(p);
     BB_CHECK_LAUNCH("route_col_kernel");
   }
-  if (a->budget > 0) return topk_sorted(p.col, a->heads, a->n, a->budget, a->out_idx, a->so_h, stream);
+  if (a->budget > 0) return topk_sorted(p.col, a->heads, a->n, a->budget, a->out_idx, false, a->so_h, stream);
   return BB_OK;
 }
 
@@ -611,10 +612,13 @@ int launch_routes_d(const bb_routes_args* a, const RtPlan& pl, char* ws, cudaStr
 
 // The k largest of each of `rows` rows of n fp32 values, positions ascending (ties at the cut in
 // position order), one CTA a row: rows too long for the cluster kernel of topk.cu.
-int topk_single(const float* vals, int64_t rows, int64_t n, int64_t k, int32_t* out, int64_t so_h,
+int topk_single(const float* vals, int64_t rows, int64_t n, int64_t k, void* out, bool out64, int64_t so_h,
                 cudaStream_t stream) {
   if (k <= 0 || rows <= 0) return BB_OK;
-  route_topk_kernel<<<(unsigned)rows, TK_THREADS, 0, stream>>>(vals, n, k, out, so_h);
+  if (out64)
+    route_topk_kernel<<<(unsigned)rows, TK_THREADS, 0, stream>>>(vals, n, k, static_cast<int64_t*>(out), so_h);
+  else
+    route_topk_kernel<<<(unsigned)rows, TK_THREADS, 0, stream>>>(vals, n, k, static_cast<int32_t*>(out), so_h);
   BB_CHECK_LAUNCH("route_topk_kernel");
   return BB_OK;
 }

@@ -29,7 +29,7 @@ namespace cg = cooperative_groups;
 
 namespace bb {
 
-int topk_single(const float* vals, int64_t rows, int64_t n, int64_t k, int32_t* out, int64_t so_h,
+int topk_single(const float* vals, int64_t rows, int64_t n, int64_t k, void* out, bool out64, int64_t so_h,
                 cudaStream_t stream);
 
 namespace {
@@ -82,8 +82,9 @@ struct TcSmem {
   int64_t sel_rem, sel_cnt;
 };
 
+template <typename OutT>
 __global__ void __launch_bounds__(TC_THREADS) topk_cluster_kernel(const float* __restrict__ vals, int64_t n,
-                                                                  int64_t k, int32_t* __restrict__ out,
+                                                                  int64_t k, OutT* __restrict__ out,
                                                                   int64_t so_h, int64_t seg) {
   cg::cluster_group cluster = cg::this_cluster();
   const int C = (int)cluster.num_blocks();
@@ -215,13 +216,13 @@ __global__ void __launch_bounds__(TC_THREADS) topk_cluster_kernel(const float* _
   const int sel_before = excl_scan(gt + eq_take_t, sm.wsum, sel_total);
   int64_t pos = off + sel_before;
   int eq_seen = 0;
-  int32_t* o = out + row * so_h;
+  OutT* o = out + row * so_h;
   for (int i = t0; i < t1; ++i) {
     const uint32_t u = keys[pad(i)] & pmask;
     bool take = u > prefix;
     if (u == prefix) take = eq_seen++ < eq_take_t;
     if (take) {
-      if (pos < k) o[pos] = (int32_t)(lo + i);
+      if (pos < k) o[pos] = (OutT)(lo + i);
       ++pos;
     }
   }
@@ -230,20 +231,13 @@ __global__ void __launch_bounds__(TC_THREADS) topk_cluster_kernel(const float* _
 
 }  // namespace
 
-// The k largest of each of `rows` rows of n fp32 values, positions ascending (ties at the cut in
-// position order): the routing top-k, also used by KV eviction and decode routing.
-int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, int32_t* out, int64_t so_h,
-                cudaStream_t stream) {
-  if (k <= 0 || rows <= 0 || n <= 0) return BB_OK;
-  // Cluster size: enough CTAs to cover the SMs, segments of at least 4096 keys, at most 16.
-  int C = 1;
-  while (C < TC_MAX_CLUSTER && rows * C < num_sms() && n / (2 * C) >= 4096) C *= 2;
-  while (C < TC_MAX_CLUSTER && cdiv(n, C) > TC_SEG_MAX) C *= 2;
-  const int64_t seg = cdiv(n, C);
-  if (C == 1 || seg > TC_SEG_MAX || rows * C > 65535) return topk_single(vals, rows, n, k, out, so_h, stream);
+// One cluster of C CTAs per row; a launch the device refuses falls back to the single-CTA kernel.
+template <typename OutT>
+int launch_cluster(const float* vals, int64_t rows, int64_t n, int64_t k, OutT* out, int64_t so_h, int C,
+                   int64_t seg, cudaStream_t stream) {
   const size_t smem = (size_t)(seg + seg / 32 + 1) * 4;
-  cudaFuncSetAttribute(topk_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (C > 8) cudaFuncSetAttribute(topk_cluster_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaFuncSetAttribute(topk_cluster_kernel<OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (C > 8) cudaFuncSetAttribute(topk_cluster_kernel<OutT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(rows * C));
   cfg.blockDim = dim3(TC_THREADS);
@@ -256,13 +250,29 @@ int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, int32_t* 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, topk_cluster_kernel, vals, n, k, out, so_h, seg);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, topk_cluster_kernel<OutT>, vals, n, k, out, so_h, seg);
   if (e != cudaSuccess) {
     (void)cudaGetLastError();
-    return topk_single(vals, rows, n, k, out, so_h, stream);
+    return topk_single(vals, rows, n, k, out, sizeof(OutT) == 8, so_h, stream);
   }
   count_launch();
   return BB_OK;
+}
+
+// The k largest of each of `rows` rows of n fp32 values, positions ascending (ties at the cut in
+// position order): the routing top-k, also used by KV eviction and decode routing. `out` holds
+// int32 positions, or int64 when out64.
+int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, void* out, bool out64, int64_t so_h,
+                cudaStream_t stream) {
+  if (k <= 0 || rows <= 0 || n <= 0) return BB_OK;
+  // Cluster size: enough CTAs to cover the SMs, segments of at least 4096 keys, at most 16.
+  int C = 1;
+  while (C < TC_MAX_CLUSTER && rows * C < num_sms() && n / (2 * C) >= 4096) C *= 2;
+  while (C < TC_MAX_CLUSTER && cdiv(n, C) > TC_SEG_MAX) C *= 2;
+  const int64_t seg = cdiv(n, C);
+  if (C == 1 || seg > TC_SEG_MAX || rows * C > 65535) return topk_single(vals, rows, n, k, out, out64, so_h, stream);
+  return out64 ? launch_cluster(vals, rows, n, k, static_cast<int64_t*>(out), so_h, C, seg, stream)
+               : launch_cluster(vals, rows, n, k, static_cast<int32_t*>(out), so_h, C, seg, stream);
 }
 
 }  // namespace bb
