@@ -1,7 +1,7 @@
 """Generate the golden vectors in this folder by running the REFERENCE implementation itself.
 
 Run once in a container that has the reference checkout (read-only) at ``$BB_REFERENCE``
-(default ``/root/reference``)::
+(default: the checkout's mount point in the build container, ``REF`` below)::
 
     PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py
 
