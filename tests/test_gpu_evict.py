@@ -28,17 +28,21 @@ def check_gather(pos, k, v, kk, vv):
     assert torch.equal(vv, v.gather(1, gi))
 
 
-@pytest.mark.parametrize("knobs", [dict(), dict(keep=3000), dict(pool=8), dict(pool_back=8), dict(pool=4, pool_back=3)],
+@pytest.mark.parametrize("knobs", [dict(), dict(keep=3000), dict(pool=8), dict(pool_back=8), dict(pool=4, pool_back=3),
+                                   dict(unsorted=1), dict(budget=4096)],
                          ids=lambda k: ",".join(f"{a}={b}" for a, b in k.items()) or "default")
 def test_kv_evict_kernel_matches_oracle(knobs):
+    """Every policy knob against the oracle, plus routes in no particular order and a budget of
+    4096 routes per head (16384 per KV-head group)."""
     from utmist_bigger_bird_b200 import _ops
-    H, hk, n, d, budget, sink, w = 32, 8, 32768, 128, 512, 64, 4096
+    H, hk, n, d, sink, w = 32, 8, 32768, 128, 64, 4096
+    budget = knobs.get("budget", 512)
     g = torch.Generator(device=DEV).manual_seed(7)
     col = torch.rand(H, n, device=DEV, generator=g) * 1e-4
     col[:, :sink] = -1
     col[:, n - w:] = -1
     idx = torch.stack([torch.randperm(n - sink - w, device=DEV, generator=g)[:budget] + sink for _ in range(H)])
-    idx = idx.sort(-1).values.to(torch.int32)
+    idx = (idx if knobs.get("unsorted") else idx.sort(-1).values).to(torch.int32)
     k = torch.randn(hk, n, d, device=DEV, generator=g).to(torch.bfloat16)
     v = torch.randn(hk, n, d, device=DEV, generator=g).to(torch.bfloat16)
     keep = knobs.get("keep", (H // hk) * budget)
