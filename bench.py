@@ -333,7 +333,15 @@ def run_ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
     cfg = CONFIGS[args.config]
-    kv_heads = kv_head_shard(rank, world, cfg.kv_heads)
+    shard_r, shard_n = rank, world
+    if args.kv_shard:
+        # One rank's share of an N-GPU run, alone on this GPU (no process group, no other ranks).
+        if world > 1:
+            raise SystemExit("--kv-shard times one rank's share on one GPU: launch it without torchrun")
+        shard_r, shard_n = (int(x) for x in args.kv_shard.split("/"))
+        if not 0 <= shard_r < shard_n:
+            raise SystemExit("--kv-shard R/N needs 0 <= R < N")
+    kv_heads = kv_head_shard(shard_r, shard_n, cfg.kv_heads)
     per = len(kv_heads)
     g = cfg.heads // cfg.kv_heads
     H = per * g
@@ -405,7 +413,14 @@ def run_ours(args):
     main_flops = 4.0 * d * float(main_pass_pairs(n, cfg.sink, cfg.window, cfg.exact_tail, idx.cpu().numpy()))
     pk, pk_kind = peaks()
     achieved = main_flops / (main_ms * 1e-3) / 1e12
-    traffic = measured_traffic()
+    # The committed ncu figure is for config 2's full launch (8 KV heads); a shard's launch moves its
+    # share of that traffic (each KV head's K/V and its query heads' Q and output), other configs none.
+    traffic = measured_traffic() if cfg.name == "config2" else None
+    traffic_src = None
+    if traffic is not None:
+        traffic *= per / cfg.kv_heads
+        traffic_src = "ncu dram bytes of the config2 main-pass launch" + (
+            "" if per == cfg.kv_heads else f", scaled to {per} of {cfg.kv_heads} KV heads")
     route_bytes = per * n * d * 2 + H * min(cfg.n_route, n) * d * 2 + H * budget * 4
     route_gbs = route_bytes / (route_ms * 1e-3) / 1e9
 
@@ -499,12 +514,16 @@ def run_ours(args):
         "config": {"workload": f"{cfg.name}: one sparse-prefill attention layer (RoPE + routes + main + exact tail)",
                    "n": n, "q_heads": cfg.heads, "kv_heads": cfg.kv_heads, "head_dim": d, "sink": cfg.sink,
                    "window": cfg.window, "vertical": cfg.vertical, "exact_tail": cfg.exact_tail,
-                   "n_route": cfg.n_route, "parallelism": f"kv-head shards x{world}",
+                   "n_route": cfg.n_route,
+                   "parallelism": (f"kv-head shards x{world}" if not args.kv_shard else
+                                   f"kv-head shard {shard_r} of {shard_n} alone on 1 GPU (the per-rank step of "
+                                   f"a {shard_n}-GPU run)"),
                    "l2": "inputs (%.2f GB per rank) exceed L2; no flush" % ((q.numel() + k.numel() + v.numel()) * 2 / 1e9),
                    "flops_per_step": flops_all},
         "roofline": {"bound": "tensor", "kernel": "flash main pass (sink+window+routed)", "achieved": achieved,
                      "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
-                     "peak_kind": f"{pk_kind} bf16 burst", "traffic": traffic, "launch_ms": main_ms,
+                     "peak_kind": f"{pk_kind} bf16 burst", "traffic": traffic, "traffic_source": traffic_src,
+                     "launch_ms": main_ms,
                      "flops_per_launch": main_flops},
         "routing": {"bound": "hbm", "ms": route_ms, "achieved_gbs": route_gbs, "peak_gbs": pk["hbm_gbs"],
                     "frac": route_gbs / pk["hbm_gbs"], "algorithmic_bytes": route_bytes},
@@ -650,6 +669,10 @@ def main():
     p.add_argument("--config", default="config2", choices=sorted(CONFIGS))
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    p.add_argument("--kv-shard", default=None, metavar="R/N",
+                   help="time rank R's share of an N-way KV-head split alone on this one GPU (no process "
+                        "group): the per-rank step of --gpus N, for a config whose whole layer needs more "
+                        "GPUs (or memory) than one")
     p.add_argument("--part", default="all", choices=["all", "decode", "evict", "model"],
                    help="time one side path alone (1 GPU) instead of the full benchmark; 'model' = the "
                         "whole-model prefill with and without the sparse path and memory savers")

@@ -61,6 +61,9 @@ CONFIGS = {
     # the headline 128K Llama-3-8B-shaped layer (bf16).
     "config2": LayerConfig("config2", 131072, torch.bfloat16, 1, 0.5, 32, 64, None, 64, 16384, 512, 256),
 }
+# configs[4]'s attention layer at 1M tokens (64 planted keys per KV head): on one GPU, run as one
+# rank's share of the 8-GPU head split (bench.py --config config5 --kv-shard R/8).
+CONFIGS["config5"] = LayerConfig("config5", 1048576, torch.bfloat16, 1, 0.5, 64, 64, None, 64, 16384, 512, 256)
 for _n in (16384, 32768, 65536, 131072, 262144, 524288):
     for _w in (4096, 16384):
         CONFIGS[f"sweep_n{_n}_w{_w}"] = _sweep(_n, _w)
