@@ -47,6 +47,36 @@ def peaks():
     return FALLBACK, "fallback"
 
 
+def parse_kv_shard(spec, rank, world):
+    """(rank, ranks) of the KV-head split whose share this process times: the launch's own
+    (RANK, WORLD_SIZE), or R/N from --kv-shard, one rank's share of an N-GPU run alone on this GPU
+    (no process group, so it cannot be combined with torchrun)."""
+    if not spec:
+        return rank, world
+    if world > 1:
+        raise SystemExit("--kv-shard times one rank's share on one GPU: launch it without torchrun")
+    try:
+        r, n = (int(x) for x in spec.split("/"))
+    except ValueError:
+        raise SystemExit(f"--kv-shard wants R/N, got {spec!r}") from None
+    if not 0 <= r < n:
+        raise SystemExit("--kv-shard R/N needs 0 <= R < N")
+    return r, n
+
+
+def main_traffic(cfg, kv_heads_here):
+    """(DRAM bytes per main-pass launch, where the figure comes from), or (None, None). The committed
+    ncu figure is for config 2's full launch; a launch over some of its KV heads moves that share of
+    it (each KV head's K/V and its query heads' Q and output); other configs have no capture."""
+    traffic = measured_traffic() if cfg.name == "config2" else None
+    if traffic is None:
+        return None, None
+    src = "ncu dram bytes of the config2 main-pass launch"
+    if kv_heads_here != cfg.kv_heads:
+        src += f", scaled to {kv_heads_here} of {cfg.kv_heads} KV heads"
+    return traffic * kv_heads_here / cfg.kv_heads, src
+
+
 def measured_traffic():
     """Per-launch DRAM bytes of the main attention kernel from the committed ncu summary."""
     if not TRAFFIC_FILE.exists():
@@ -333,14 +363,7 @@ def run_ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
     cfg = CONFIGS[args.config]
-    shard_r, shard_n = rank, world
-    if args.kv_shard:
-        # One rank's share of an N-GPU run, alone on this GPU (no process group, no other ranks).
-        if world > 1:
-            raise SystemExit("--kv-shard times one rank's share on one GPU: launch it without torchrun")
-        shard_r, shard_n = (int(x) for x in args.kv_shard.split("/"))
-        if not 0 <= shard_r < shard_n:
-            raise SystemExit("--kv-shard R/N needs 0 <= R < N")
+    shard_r, shard_n = parse_kv_shard(args.kv_shard, rank, world)
     kv_heads = kv_head_shard(shard_r, shard_n, cfg.kv_heads)
     per = len(kv_heads)
     g = cfg.heads // cfg.kv_heads
@@ -413,14 +436,7 @@ def run_ours(args):
     main_flops = 4.0 * d * float(main_pass_pairs(n, cfg.sink, cfg.window, cfg.exact_tail, idx.cpu().numpy()))
     pk, pk_kind = peaks()
     achieved = main_flops / (main_ms * 1e-3) / 1e12
-    # The committed ncu figure is for config 2's full launch (8 KV heads); a shard's launch moves its
-    # share of that traffic (each KV head's K/V and its query heads' Q and output), other configs none.
-    traffic = measured_traffic() if cfg.name == "config2" else None
-    traffic_src = None
-    if traffic is not None:
-        traffic *= per / cfg.kv_heads
-        traffic_src = "ncu dram bytes of the config2 main-pass launch" + (
-            "" if per == cfg.kv_heads else f", scaled to {per} of {cfg.kv_heads} KV heads")
+    traffic, traffic_src = main_traffic(cfg, per)
     route_bytes = per * n * d * 2 + H * min(cfg.n_route, n) * d * 2 + H * budget * 4
     route_gbs = route_bytes / (route_ms * 1e-3) / 1e9
 
