@@ -38,7 +38,19 @@ from utmist_bigger_bird_b200.workload import CONFIGS, make_layer  # noqa: E402
 
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-TRAFFIC_FILE = ROOT / "profiles" / "flash_main_config2.md"
+KERNEL_SOURCES = [ROOT / "utmist_bigger_bird_b200" / "csrc" / f for f in ("flash_tc.cu", "tc_common.cuh")]
+# DRAM traffic of the main-pass kernel, from one ncu capture (dram__bytes_read.sum +
+# dram__bytes_write.sum) of config 2's main pass, and the hash of the kernel sources it was taken
+# on. When the sources change the figure no longer describes the kernel and the bench reports null.
+MAIN_TRAFFIC = {"sources_sha256": None, "bytes_per_launch": None, "capture": None}
+
+
+def sources_sha256():
+    import hashlib
+    h = hashlib.sha256()
+    for f in KERNEL_SOURCES:
+        h.update(f.read_bytes())
+    return h.hexdigest()[:16]
 
 
 def peaks():
@@ -64,30 +76,31 @@ def parse_kv_shard(spec, rank, world):
     return r, n
 
 
-def main_traffic(cfg, kv_heads_here):
-    """(DRAM bytes per main-pass launch, where the figure comes from), or (None, None). The committed
-    ncu figure is for config 2's full launch; a launch over some of its KV heads moves that share of
-    it (each KV head's K/V and its query heads' Q and output); other configs have no capture."""
-    traffic = measured_traffic() if cfg.name == "config2" else None
-    if traffic is None:
-        return None, None
-    src = "ncu dram bytes of the config2 main-pass launch"
+def main_traffic(cfg, kv_heads_here, sha=None):
+    """(DRAM bytes per main-pass launch, where the figure comes from), or (None, why not). The
+    committed ncu figure is for config 2's full launch on the kernel sources whose hash it carries; a
+    launch over some of its KV heads moves that share of it (each KV head's K/V and its query heads'
+    Q and output); other configs, and changed sources, have no capture."""
+    if cfg.name != "config2":
+        return None, f"no ncu capture of {cfg.name}"
+    sha = sha or sources_sha256()
+    if MAIN_TRAFFIC["bytes_per_launch"] is None or MAIN_TRAFFIC["sources_sha256"] != sha:
+        return None, f"no ncu capture of the current kernel sources ({sha})"
+    src = f"ncu dram bytes of the config2 main-pass launch ({MAIN_TRAFFIC['capture']}; sources {sha})"
     if kv_heads_here != cfg.kv_heads:
         src += f", scaled to {kv_heads_here} of {cfg.kv_heads} KV heads"
-    return traffic * kv_heads_here / cfg.kv_heads, src
+    return MAIN_TRAFFIC["bytes_per_launch"] * kv_heads_here / cfg.kv_heads, src
 
 
-def measured_traffic():
-    """Per-launch DRAM bytes of the main attention kernel from the committed ncu summary."""
-    if not TRAFFIC_FILE.exists():
-        return None
-    for line in TRAFFIC_FILE.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].split()[0])
-            except ValueError:
-                return None
-    return None
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
 
 
 # ----------------------------------------------------------------------------- FLOP counting
@@ -236,9 +249,10 @@ def run_reference(args):
     line = {"impl": "reference", "metric": "eff_tflops_sparse_prefill_layer", "value": value, "unit": "TFLOP/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": total / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
             "config": {"workload": cfg.name, "n": cfg.n, "sample": "bounded CPU sample (see cpu_baseline)"},
-            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "cpu": cpu_model(), "kind": "port",
+                             "dtype": "fp32", "sample": sample},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -347,6 +361,79 @@ def side_paths(cfg, qr, kr, v, idx, qpos, budget, dev, stream, reps, pk, parts=(
     return evict_line, decode_line
 
 
+def host_link(q_h, k_h, v_h, cos_h, sin_h, out_h, buf, s_in, s_out, steps, dev, world, local):
+    """The host link alone: the e2e step's H2D copies (pinned q/k/v/cos/sin) on one stream and its
+    D2H copy of the output on another, concurrently, with no compute, on every rank at once (the
+    ranks share the host's links). Returns the per-step time (max over ranks) and rates; the e2e
+    step cannot be faster than this."""
+    import torch.distributed as dist
+    from utmist_bigger_bird_b200.sharding import reduce_step
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize(dev)
+    t0 = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    t1 = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    start = torch.cuda.Event()
+    start.record(s_in)
+    s_out.wait_event(start)
+    t0[0].record(s_in)
+    t0[1].record(s_out)
+    for _ in range(steps):
+        with torch.cuda.stream(s_in):
+            for name, src in (("q", q_h), ("k", k_h), ("v", v_h), ("cos", cos_h), ("sin", sin_h)):
+                buf[name].copy_(src, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            out_h.copy_(buf["out"].permute(1, 0, 2), non_blocking=True)
+    t1[0].record(s_in)
+    t1[1].record(s_out)
+    torch.cuda.synchronize(dev)
+    h2d_ms = t0[0].elapsed_time(t1[0]) / steps
+    d2h_ms = t0[1].elapsed_time(t1[1]) / steps
+    ms, _ = reduce_step(max(h2d_ms, d2h_ms), 0.0, dev)
+    h2d = sum(t.numel() * t.element_size() for t in (q_h, k_h, v_h, cos_h, sin_h))
+    d2h = out_h.numel() * out_h.element_size()
+    return {"ms_per_step": ms, "h2d_gbs": h2d / (h2d_ms * 1e-3) / 1e9, "d2h_gbs": d2h / (d2h_ms * 1e-3) / 1e9,
+            "note": "H2D and D2H of one e2e step's bytes concurrently on this rank, no compute, all ranks at once; "
+                    "ms_per_step = max over ranks of the slower direction"}
+
+
+def collectives(n, w_local, hidden, dev, stream, world, local, reps=5):
+    """The whole-model step's exchanges for one layer at this layer's size (n tokens), on the
+    launch's process group: the all-gather of the ranks' head outputs [n, w_local] bf16 before a
+    replicated o_proj (``sharding.GatheredOProj``, with its projection), and the all-reduce of
+    [n, hidden] bf16 after the row-parallel o_proj or MLP down projection
+    (``sharding.RowParallelLinear``). Device time with CUDA events, max over ranks; bus rates
+    use NCCL's conventions ((P-1)/P of the gathered bytes; 2(P-1)/P of the reduced bytes)."""
+    import torch.distributed as dist
+    from utmist_bigger_bird_b200.sharding import GatheredOProj, reduce_step
+    x = torch.randn(n, w_local, device=dev, dtype=torch.bfloat16)
+    gathered = torch.empty(world * n, w_local, device=dev, dtype=torch.bfloat16)
+    red = torch.randn(n, hidden, device=dev, dtype=torch.bfloat16)
+    o_proj = torch.nn.Linear(world * w_local, hidden, bias=False, device=dev, dtype=torch.bfloat16)
+    gproj = GatheredOProj(o_proj, world)
+    ops = {"all_gather": lambda: dist.all_gather_into_tensor(gathered, x),
+           "all_reduce": lambda: dist.all_reduce(red),
+           "gathered_o_proj": lambda: gproj(x)}
+    out = {}
+    for name, fn in ops.items():
+        fn()
+        dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+        ms, _ = reduce_step(event_time(fn, reps, stream), 0.0, dev)
+        out[name] = {"ms": ms}
+    frac = (world - 1) / world
+    ag_bytes = world * n * w_local * 2
+    ar_bytes = n * hidden * 2
+    out["all_gather"].update(bytes=ag_bytes, bus_gbs=ag_bytes * frac / (out["all_gather"]["ms"] * 1e-3) / 1e9)
+    out["all_reduce"].update(bytes=ar_bytes, bus_gbs=2 * ar_bytes * frac / (out["all_reduce"]["ms"] * 1e-3) / 1e9)
+    out["gathered_o_proj"].update(flops=2.0 * n * world * w_local * hidden)
+    out["note"] = (f"one layer's exchange at n={n}: all-gather of [n, {w_local}] bf16 per rank (before the replicated "
+                   f"o_proj), all-reduce of [n, {hidden}] bf16 (after a row-parallel o_proj or MLP); NCCL over NVLink")
+    del x, gathered, red, o_proj, gproj
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args):
     import torch.distributed as dist
 
@@ -389,13 +476,31 @@ def run_ours(args):
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize(dev)
 
+    def restore():
+        # The step applies RoPE to q/k in place: give every step the stated (pre-RoPE) inputs.
+        q.copy_(q0)
+        k.copy_(k0)
+
+    def timed_steps(steps):
+        """Mean device time of ``step`` over ``steps`` steps, each on freshly restored inputs; the
+        restoring copies sit between the timed events."""
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for s_ev, e_ev in evs:
+            restore()
+            s_ev.record(stream)
+            step()
+            e_ev.record(stream)
+        evs[-1][1].synchronize()
+        return sum(s_ev.elapsed_time(e_ev) for s_ev, e_ev in evs) / steps
+
     for _ in range(max(args.warmup, 3)):
+        restore()
         step()
     barrier()
     launches0 = L.bb_kernel_launches()
     with ClockSampler(dev) as clocks:
         barrier()
-        ms = event_time(step, args.steps, stream)
+        ms = timed_steps(args.steps)
         barrier()
     launches = L.bb_kernel_launches() - launches0
     clock = clocks.summary()
@@ -507,6 +612,11 @@ def run_ours(args):
     e2e_ms = t_start.elapsed_time(t_end) / e2e_steps
     e2e_max, _ = reduce_step(e2e_ms, 0.0, dev)
     e2e_value = flops_all / (e2e_max * 1e-3) / 1e12
+    link = host_link(q_h, k_h, v_h, cos_h, sin_h, out_h[0], bufs[0], s_in, s_out, e2e_steps, dev, world, local)
+    link["e2e_frac"] = link["ms_per_step"] / e2e_max
+    del bufs, out_h
+    torch.cuda.empty_cache()
+    coll = collectives(n, H * d, cfg.heads * d, dev, stream, world, local) if world > 1 else None
 
     # ---- CPU baseline (rank 0, N = 1 only)
     cpu = None
@@ -514,7 +624,8 @@ def run_ours(args):
         threads = os.cpu_count() or 1
         torch.set_num_threads(threads)
         dt, fl = cpu_sample(cfg)
-        cpu = {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+        cpu = {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "cpu": cpu_model(), "kind": "port",
+               "dtype": "fp32",
                "sample": f"routes of KV head 0 over all {n} keys + 48 spread/tail query rows x 2 query heads, "
                          f"numpy oracle port ({dt:.1f} s)"}
 
@@ -523,8 +634,10 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return
+    metric = "eff_tflops_sparse_prefill_layer" + ("_rank_share" if args.kv_shard else "")
     line = {
-        "metric": "eff_tflops_sparse_prefill_layer", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "metric": metric, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "kv_shard": args.kv_shard,
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_max, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"{cfg.name}: one sparse-prefill attention layer (RoPE + routes + main + exact tail)",
@@ -551,7 +664,9 @@ def run_ours(args):
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms": e2e_max, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "note": "pipelined serving loop: H2D of step i+1 and D2H of step i-1 overlap step i; "
-                        "the first H2D and last D2H are inside the timed region"},
+                        "the first H2D and last D2H are inside the timed region",
+                "host_link": link},
+        "collectives": coll,
         "gpu_launches": int(launches),
         "clocks": clock,
         "gpu": torch.cuda.get_device_name(dev),

@@ -64,6 +64,16 @@ BB_API uint64_t bb_kernel_launches(void);
  * copies, frees its tensor memory and returns instead of hanging. Synchronous (copies 4 bytes
  * from the device). No counterpart in the reference. */
 BB_API int bb_device_fault(int* code);
+/* Sets the limit of every bounded wait of this library's kernels on the current device (ns > 0;
+ * 2e9 by default), for launches made after the call. A shorter limit makes a kernel give up
+ * sooner when another warp stops making progress. Synchronous. No counterpart in the reference. */
+BB_API int bb_set_wait_limit_ns(uint64_t ns);
+/* Test hook of the attention kernels' abort path (off by default). While on, the MMA warp of
+ * every tcgen05 attention CTA (bb_flash, bb_sparse_prefill with head_dim 128) first waits for a
+ * barrier that nothing completes: the wait runs out after the wait limit, the launch takes its
+ * abort path (outputs of aborted tiles are zeros, copies drained, tensor memory freed) and
+ * bb_device_fault then reports code 9. Synchronous. No counterpart in the reference. */
+BB_API int bb_debug_stall_attention(int on);
 
 /* ------------------------------------------------------------------------------------------
  * RoPE, in place: x[b,h,t,:] <- x*cos[b,t,:] + rotate_half(x)*sin[b,t,:], every op rounded to

@@ -23,6 +23,8 @@ What it restates (paths inside the reference project derkychen/utmist-bigger-bir
                         query rows so long sequences stay tractable.
 * ``sparse_prefill`` -- ``modal_rd/attention.py:176-206`` (routes, optional ``vertical_scope``
                         groups, main pass, exact tail overwriting the last ``exact_tail`` rows).
+                        ``route_scores_at`` / ``flash_at`` / ``sparse_prefill_at`` are the same
+                        arithmetic given only the query rows to evaluate (long prompts).
 * ``decode``         -- ``kernels/bigger_bird_decode.py:21-107``: one query per head over the virtual
                         key list front | window | routed (positions outside [0, n) skipped; a key
                         listed twice counts twice, as in the kernel), exact softmax in fp32.
@@ -45,7 +47,8 @@ import numpy as np
 
 __all__ = [
     "bf16_round", "f16_round", "rounder", "rope", "vertical_budget", "route_query_positions",
-    "route_scores", "routes", "topk_sorted", "route_sets_match", "flash", "sparse_prefill",
+    "route_scores", "route_scores_at", "routes", "topk_sorted", "route_sets_match", "flash", "flash_at",
+    "sparse_prefill", "sparse_prefill_at",
     "forward_pool", "evict_positions", "decode", "pooled_probs",
 ]
 
@@ -129,13 +132,23 @@ def route_scores(q, k, *, scaling, sink, window, n_route=64, pool="mean", querie
     q: [H, n, d], k: [Hk, n, d] float32 arrays holding ``dtype`` values (post-RoPE).
     ``modal_rd/attention.py:148-170``."""
     q = np.asarray(q, dtype=np.float32)
-    k = np.asarray(k, dtype=np.float32)
     H, n, d = q.shape
-    hk = k.shape[0]
-    g = H // hk
     r = min(n_route, n)
     if qpos is None:
         qpos = route_query_positions(n, r, queries, sink, window)
+    qpos = np.asarray(qpos, dtype=np.int64)
+    return route_scores_at(q[:, qpos, :], k, qpos, scaling=scaling, sink=sink, window=window, pool=pool,
+                           dtype=dtype)
+
+
+def route_scores_at(q_sel, k, qpos, *, scaling, sink, window, pool="mean", dtype="bf16"):
+    """``route_scores`` given only the routing query rows: q_sel [H, r, d] holds the rows at
+    positions ``qpos`` (so a long prompt's full Q is not needed); k: [Hk, n, d]."""
+    q_sel = np.asarray(q_sel, dtype=np.float32)
+    k = np.asarray(k, dtype=np.float32)
+    H, r, d = q_sel.shape
+    hk, n, _ = k.shape
+    g = H // hk
     qpos = np.asarray(qpos, dtype=np.int64)
     rnd = rounder(dtype)
     keypos = np.arange(n)
@@ -143,7 +156,7 @@ def route_scores(q, k, *, scaling, sink, window, n_route=64, pool="mean", querie
     masked = keypos[None, :] > qpos_g[:, None]
     col = np.zeros((H, n), dtype=np.float32)
     for h in range(hk):
-        qa = q[h * g:(h + 1) * g][:, qpos, :].reshape(g * r, d)
+        qa = q_sel[h * g:(h + 1) * g].reshape(g * r, d)
         s = (qa.astype(np.float64) @ k[h].astype(np.float64).T).astype(np.float32)
         s = rnd(s) * np.float32(scaling)
         s[masked] = -np.inf
@@ -224,27 +237,41 @@ def flash(q, k, v, indices, *, front=64, window=256, token_mask=None, num_heads=
     (local indices into T) and ``heads`` selects query heads; the result is
     ``[len(heads), len(rows), D]`` float32 (not rounded to the input dtype)."""
     q = np.asarray(q, dtype=np.float32)
-    k = np.asarray(k, dtype=np.float32)
-    v = np.asarray(v, dtype=np.float32)
     bh, t, d = q.shape
-    n = k.shape[1]
+    n = np.shape(k)[1]
     offset = n - t
     if offset < 0:
         raise ValueError("Key sequence must be at least as long as query sequence")
+    rows = np.arange(t) if rows is None else np.asarray(rows, dtype=np.int64)
+    heads = np.arange(bh) if heads is None else np.asarray(heads, dtype=np.int64)
+    return flash_at(q[heads][:, rows], rows + offset, k, v, indices, heads=heads, front=front, window=window,
+                    token_mask=token_mask, num_heads=num_heads, route_chunk=route_chunk, kv_groups=kv_groups,
+                    scale=scale)
+
+
+def flash_at(q_rows, qs, k, v, indices, *, heads, front=64, window=256, token_mask=None, num_heads=32,
+             route_chunk=None, kv_groups=1, scale=1.0):
+    """``flash`` given only the query rows to compute: q_rows [len(heads), R, D] are the rows of
+    query heads ``heads`` at absolute positions ``qs`` [R]; k/v [BH/kv_groups, N, D]; indices as in
+    ``flash`` (indexed by query head). Returns [len(heads), R, D] float32."""
+    q_rows = np.asarray(q_rows, dtype=np.float32)
+    k = np.asarray(k, dtype=np.float32)
+    v = np.asarray(v, dtype=np.float32)
+    n = k.shape[1]
+    d = q_rows.shape[-1]
     idx_all = np.asarray(indices)
     if idx_all.ndim == 2:
         idx_all = idx_all[:, None, :]
     route_chunk = route_chunk or n
     front = min(front, n)
-    rows = np.arange(t) if rows is None else np.asarray(rows, dtype=np.int64)
-    heads = np.arange(bh) if heads is None else np.asarray(heads, dtype=np.int64)
-    qs = rows + offset
+    qs = np.asarray(qs, dtype=np.int64)
+    heads = np.asarray(heads, dtype=np.int64)
     kp = np.arange(n)
     causal = kp[None, :] <= qs[:, None]
     base = causal & ((kp[None, :] < front) | (kp[None, :] > qs[:, None] - window))
     beyond = kp[None, :] < qs[:, None] - window + 1
     group = qs // route_chunk
-    out = np.zeros((len(heads), len(rows), d), dtype=np.float32)
+    out = np.zeros((len(heads), len(qs), d), dtype=np.float32)
     for oi, h in enumerate(heads):
         kv = _kv_head(int(h), num_heads, kv_groups)
         idx = idx_all[h].astype(np.int64)                         # [G, K]
@@ -257,7 +284,7 @@ def flash(q, k, v, indices, *, front=64, window=256, token_mask=None, num_heads=
         if token_mask is not None:
             b = int(h) // num_heads
             mask &= np.asarray(token_mask[b], dtype=bool)[None, :]
-        s = (q[h, rows] @ k[kv].T) * np.float32(scale)
+        s = (q_rows[oi] @ k[kv].T) * np.float32(scale)
         s = np.where(mask, s, -np.inf).astype(np.float32)
         m = s.max(-1, keepdims=True)
         m = np.where(np.isfinite(m), m, 0.0).astype(np.float32)
@@ -306,6 +333,36 @@ def sparse_prefill(q, k, v, *, scaling, sink, window, vertical, vertical_sqrt=0.
                          kv_groups=g, scale=scaling, rows=rows[tail_rows] - (n - r), heads=heads)
             out[:, tail_rows] = tail
     return out, idx
+
+
+def sparse_prefill_at(q_rows, qs, k, v, idx, *, heads, scaling, sink, window, exact_tail=0,
+                      vertical_scope=0, scope_chunk=4096):
+    """``sparse_prefill`` output for the query rows ``q_rows [len(heads), R, d]`` at absolute
+    positions ``qs`` with routes ``idx [H, budget]`` given: rows at or after ``n - exact_tail``
+    take the exact causal tail, the others the main pass. Returns [len(heads), R, d] fp32."""
+    H = np.shape(idx)[0]
+    hk, n, _ = np.shape(k)
+    g = H // hk
+    qs = np.asarray(qs, dtype=np.int64)
+    idx = np.asarray(idx)
+    if vertical_scope:
+        chunk = scope_chunk
+        groups = -(-n // chunk)
+        starts = np.arange(groups) * chunk
+        active = (starts + chunk > n - vertical_scope)[None, :, None]
+        routed = np.where(active, idx[:, None, :], -1)
+    else:
+        chunk, routed = None, idx[:, None, :]
+    q_rows = np.asarray(q_rows, dtype=np.float32)
+    out = flash_at(q_rows, qs, k, v, routed, heads=heads, front=sink, window=window, num_heads=H,
+                   route_chunk=chunk, kv_groups=g, scale=scaling)
+    r = min(exact_tail, n)
+    tail = qs >= n - r
+    if r and tail.any():
+        none = -np.ones((H, 1, 1), dtype=np.int32)
+        out[:, tail] = flash_at(q_rows[:, tail], qs[tail], k, v, none, heads=heads, front=0, window=n,
+                                num_heads=H, kv_groups=g, scale=scaling)
+    return out
 
 
 # ----------------------------------------------------------------------------- KV eviction

@@ -1,9 +1,9 @@
 """Generate the golden vectors in this folder by running the REFERENCE implementation itself.
 
-Run once in a container that has the reference checkout (read-only) at ``$BB_REFERENCE``
-(default: the checkout's mount point in the build container, ``REF`` below)::
+Run once where a checkout of the reference is available (read-only), naming it with
+``BB_REFERENCE`` or as the first argument::
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py
+    PYTHONDONTWRITEBYTECODE=1 BB_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 It imports ``modal_rd.attention`` (``RDAttention``, ``rope_inplace``) and
 ``kernels.bigger_bird_flash_ref`` from the reference and runs them on the CPU (the reference's
@@ -23,7 +23,10 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF = Path(os.environ.get("BB_REFERENCE", "/root/reference"))
+_ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("BB_REFERENCE")
+if not _ref:
+    raise SystemExit("make_golden.py: name the reference checkout with BB_REFERENCE=<path> or as the first argument")
+REF = Path(_ref)
 sys.dont_write_bytecode = True
 sys.path.insert(0, str(REF))
 sys.path.insert(0, str(REPO))

@@ -1,5 +1,5 @@
-"""Host logic of bench.py that runs without a GPU: the per-rank share option and the scope of the
-main kernel's DRAM-traffic figure."""
+"""Host logic of bench.py that runs without a GPU: the per-rank share option, the scope of the main
+kernel's DRAM-traffic figure and the CPU description."""
 import pytest
 
 import bench
@@ -22,12 +22,26 @@ def test_kv_shard_rejects_bad_specs(spec, world):
         bench.parse_kv_shard(spec, 0, world)
 
 
-def test_traffic_only_for_the_captured_config():
-    full = bench.measured_traffic()
-    assert full is not None and full > 0, "profiles/flash_main_config2.md carries the ncu figure"
+def test_traffic_only_for_the_captured_kernel_and_config(monkeypatch):
+    """The committed ncu figure applies only to config 2 and only to the kernel sources it was
+    captured on; a rank's share is scaled by its KV heads."""
     cfg2 = CONFIGS["config2"]
-    assert bench.main_traffic(cfg2, cfg2.kv_heads) == (full, "ncu dram bytes of the config2 main-pass launch")
-    t, src = bench.main_traffic(cfg2, 1)
-    assert t == pytest.approx(full / cfg2.kv_heads) and "scaled to 1 of 8" in src
-    assert bench.main_traffic(CONFIGS["config5"], 1) == (None, None)
-    assert bench.main_traffic(CONFIGS["sweep_n65536_w16384"], 8) == (None, None)
+    monkeypatch.setitem(bench.MAIN_TRAFFIC, "sources_sha256", "abc")
+    monkeypatch.setitem(bench.MAIN_TRAFFIC, "bytes_per_launch", 8.0e9)
+    monkeypatch.setitem(bench.MAIN_TRAFFIC, "capture", "test")
+    t, src = bench.main_traffic(cfg2, cfg2.kv_heads, sha="abc")
+    assert t == 8.0e9 and "config2" in src
+    t, src = bench.main_traffic(cfg2, 1, sha="abc")
+    assert t == pytest.approx(1.0e9) and "scaled to 1 of 8" in src
+    t, src = bench.main_traffic(cfg2, 8, sha="other")
+    assert t is None and "current kernel sources" in src
+    assert bench.main_traffic(CONFIGS["config5"], 1, sha="abc")[0] is None
+    assert bench.main_traffic(CONFIGS["sweep_n65536_w16384"], 8, sha="abc")[0] is None
+
+
+def test_sources_hash_is_stable():
+    assert bench.sources_sha256() == bench.sources_sha256() and len(bench.sources_sha256()) == 16
+
+
+def test_cpu_model_is_named():
+    assert isinstance(bench.cpu_model(), str) and bench.cpu_model()

@@ -184,3 +184,10 @@ def test_decode_host_validation(kw, fn, msg):
     nbytes = C.c_size_t(0)
     assert getattr(L, fn)(C.byref(a), C.byref(nbytes)) != 0
     assert msg in L.bb_last_error().decode()
+
+
+def test_wait_limit_must_be_positive():
+    """bb_set_wait_limit_ns refuses 0 on the host, before touching a device."""
+    L = _lib.lib()
+    assert L.bb_set_wait_limit_ns(0) == _lib.BB_ERR_ARG
+    assert "positive" in L.bb_last_error().decode()

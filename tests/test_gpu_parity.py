@@ -142,10 +142,10 @@ def test_full_budget_equals_sdpa():
     close(np32(out), np32(dense), "full budget")
 
 
-@pytest.mark.parametrize("n", [524288, 524352])
+@pytest.mark.parametrize("n", [524224, 524288, 524352, 995993])
 def test_long_index_identity(n):
-    """modal_rd/check_long_indexing.py:40-55: window=1, no routes => out[h] == v[h // 4] exactly,
-    with [n, H, d] strided views (element offsets beyond 2^31)."""
+    """modal_rd/check_long_indexing.py:32,40-55 (the reference's four lengths): window=1, no routes
+    => out[h] == v[h // 4] exactly, with [n, H, d] strided views (element offsets beyond 2^31)."""
     from utmist_bigger_bird_b200 import bigger_bird_flash
     h, hk, d = 32, 8, 128
     q = torch.zeros((n, h, d), device=DEV, dtype=torch.bfloat16).permute(1, 0, 2)

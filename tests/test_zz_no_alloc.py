@@ -66,6 +66,6 @@ def test_routes_noalloc_matches_workspace_entry_point():
     big = _lib.RoutesArgs(heads=32, kv_heads=8, n=1 << 20, d=128, r=64, sink=64, window=2048, budget=256,
                           scaling=0.088, dtype=_lib.BB_BF16)
     status = L.bb_routes_noalloc(C.byref(big), stream)
-    assert status == 5
+    assert status == _lib.BB_ERR_WORKSPACE
     msg = L.bb_last_error().decode()
     assert "scratch" in msg and str(24 << 20) in msg

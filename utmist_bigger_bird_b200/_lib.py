@@ -13,6 +13,8 @@ LIB_PATH = Path(__file__).resolve().parent / "libbb_b200.so"
 
 BB_F16, BB_BF16, BB_F32 = 0, 1, 2
 BB_POOL_MEAN, BB_POOL_MAX = 0, 1
+(BB_OK, BB_ERR_ARG, BB_ERR_SHAPE, BB_ERR_DTYPE, BB_ERR_STRIDE, BB_ERR_WORKSPACE, BB_ERR_LAUNCH,
+ BB_ERR_UNSUPPORTED, BB_ERR_DEVICE) = range(9)
 ABI_VERSION = 2
 
 _VALUE_ERRORS = {1, 2, 3, 4, 5, 7}
@@ -96,6 +98,8 @@ EXPORTS = {
     "bb_abi_version": (C.c_int, []),
     "bb_kernel_launches": (C.c_uint64, []),
     "bb_device_fault": (C.c_int, [C.POINTER(C.c_int)]),
+    "bb_set_wait_limit_ns": (C.c_int, [C.c_uint64]),
+    "bb_debug_stall_attention": (C.c_int, [C.c_int]),
     "bb_rope_inplace": (C.c_int, [vp, C.c_int, i64, i64, i64, i64, i64, i64, i64, vp, vp, i64, i64, vp]),
     "bb_routes_workspace_size": (C.c_int, [C.POINTER(RoutesArgs), C.POINTER(C.c_size_t)]),
     "bb_routes": (C.c_int, [C.POINTER(RoutesArgs), vp, C.c_size_t, vp]),

@@ -178,6 +178,18 @@ int bb_device_fault(int* code) {
   return BB_OK;
 }
 
+int bb_set_wait_limit_ns(uint64_t ns) {
+  if (ns == 0) return bb::fail(BB_ERR_ARG, "set_wait_limit_ns: the limit must be positive");
+  if (bb::flash_set_wait_limit(ns) || bb::routes_set_wait_limit(ns) || bb::decode_set_wait_limit(ns))
+    return bb::fail(BB_ERR_LAUNCH, "set_wait_limit_ns: %s", cudaGetErrorString(cudaGetLastError()));
+  return BB_OK;
+}
+
+int bb_debug_stall_attention(int on) {
+  if (bb::flash_set_stall(on)) return bb::fail(BB_ERR_LAUNCH, "debug_stall_attention: %s", cudaGetErrorString(cudaGetLastError()));
+  return BB_OK;
+}
+
 int bb_rope_inplace(void* x, int dtype, int64_t B, int64_t H, int64_t T, int64_t D, int64_t sxb,
                     int64_t sxh, int64_t sxt, const void* cos, const void* sin, int64_t scb,
                     int64_t sct, bb_stream_t stream) {

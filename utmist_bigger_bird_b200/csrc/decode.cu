@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(DK_THREADS, 2) decode_partial_kernel(DecodePar
 #pragma unroll 1
   for (; b < nblocks; ++b) {
     const int slot = b % DK_NST;
-    const bool ok = tc::mbar_wait(smem_u32(full + slot), (uint32_t)((b / DK_NST) & 1), abort_flag, 40);
+    const bool ok = tc::mbar_wait(smem_u32(full + slot), (uint32_t)((b / DK_NST) & 1), tc::Abort{abort_flag, 0u}, 40);
     if (!__syncthreads_and(ok)) break;  // stage b landed for all; stage b - 1 is free
     issue(b + DK_NST - 1, pf);
     pf = fetch(b + DK_NST);
@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(DK_THREADS) droute_scores_kernel(DecodeParams 
 #pragma unroll 1
   for (; b < nblocks; ++b) {
     const int slot = b % DK_NST;
-    const bool ok = tc::mbar_wait(smem_u32(full + slot), (uint32_t)((b / DK_NST) & 1), abort_flag, 41);
+    const bool ok = tc::mbar_wait(smem_u32(full + slot), (uint32_t)((b / DK_NST) & 1), tc::Abort{abort_flag, 0u}, 41);
     if (!__syncthreads_and(ok)) break;
     issue(b + DK_NST - 1);
     const int32_t* ps = pos_s + slot * DK_BN;
@@ -776,7 +776,7 @@ __global__ void __launch_bounds__(DT_THREADS, 2) decode_tma_kernel(const __grid_
     int slot = 0;
     uint32_t ph = 0;
     for (int blk = 0; blk < nblocks; ++blk) {
-      if (blk >= DT_NST && !tc::mbar_wait_warp(smem_u32(c.empty + slot), ph ^ 1u, c.abort_flag, 44)) break;
+      if (blk >= DT_NST && !tc::mbar_wait_warp(smem_u32(c.empty + slot), ph ^ 1u, tc::Abort{c.abort_flag, 0u}, 44)) break;
       const int32_t p0 = f0, p1 = f1;
       f0 = fetch(blk + 1, lane);
       f1 = fetch(blk + 1, lane + 32);
@@ -800,7 +800,7 @@ __global__ void __launch_bounds__(DT_THREADS, 2) decode_tma_kernel(const __grid_
     int slot = 0;
     uint32_t ph = 0;
     for (int b = 0; b < nblocks; ++b) {
-      if (!tc::mbar_wait_warp(smem_u32(c.full + slot), ph, c.abort_flag, 45)) break;
+      if (!tc::mbar_wait_warp(smem_u32(c.full + slot), ph, tc::Abort{c.abort_flag, 0u}, 45)) break;
       const uint64_t msk = c.mask[slot];
       const uint32_t kt = ring + (uint32_t)slot * 2u * DT_TILE, vt = kt + DT_TILE;
       float s[2][4];
@@ -945,7 +945,7 @@ __global__ void __launch_bounds__(DT_THREADS) droute_tma_kernel(const __grid_con
     int slot = 0;
     uint32_t ph = 0;
     for (int blk = 0; blk < nblocks; ++blk) {
-      if (blk >= DT_NST && !tc::mbar_wait_warp(smem_u32(c.empty + slot), ph ^ 1u, c.abort_flag, 46)) break;
+      if (blk >= DT_NST && !tc::mbar_wait_warp(smem_u32(c.empty + slot), ph ^ 1u, tc::Abort{c.abort_flag, 0u}, 46)) break;
       const int64_t j = j0 + (int64_t)blk * DK_BN + lane;
       dt_produce<T>(c.mask + slot, smem_u32(c.full + slot), j < j1 ? (int32_t)j : -1,
                     j + 32 < j1 ? (int32_t)(j + 32) : -1, &maps.k, nullptr, kv * maps.k_head_rows, 0, K, p.sk_t,
@@ -966,7 +966,7 @@ __global__ void __launch_bounds__(DT_THREADS) droute_tma_kernel(const __grid_con
     int slot = 0;
     uint32_t ph = 0;
     for (int b = 0; b < nblocks; ++b) {
-      if (!tc::mbar_wait_warp(smem_u32(c.full + slot), ph, c.abort_flag, 47)) break;
+      if (!tc::mbar_wait_warp(smem_u32(c.full + slot), ph, tc::Abort{c.abort_flag, 0u}, 47)) break;
       const uint64_t msk = c.mask[slot];
       const int64_t jb = j0 + (int64_t)b * DK_BN;
       float s[2][4];
@@ -1310,6 +1310,8 @@ int decode_route(const bb_decode_args* a, void* ws, size_t ws_bytes, cudaStream_
   if (dp == 64) return launch_droute<__half, 64>(a, pl, w, stream);
   return launch_droute<__half, 128>(a, pl, w, stream);
 }
+
+int decode_set_wait_limit(unsigned long long ns) { return tc::unit_set_wait_limit(ns); }
 
 int decode_fault_take(int* code) {
   int v = 0;

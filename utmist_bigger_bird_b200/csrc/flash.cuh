@@ -25,6 +25,7 @@ struct FlashParams {
   float* part_acc;             // [splits][BH][T][128] (split mode)
   float2* part_ml;             // [splits][BH][T]: (running max in log2 units, sum)
   int64_t bh;
+  uint32_t serial;             // launch serial (cross-CTA abort of the tcgen05 kernels)
 };
 
 int flash_tc_launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream);
@@ -34,5 +35,11 @@ int flash_tc_splits(const bb_flash_args* a, int sms);
 int flash_fault_take(int* code);
 int routes_fault_take(int* code);
 int decode_fault_take(int* code);
+// Wait limit (ns) of the bounded waits of each unit's kernels, on the current device.
+int flash_set_wait_limit(unsigned long long ns);
+int routes_set_wait_limit(unsigned long long ns);
+int decode_set_wait_limit(unsigned long long ns);
+// Test hook of the attention kernels' abort path (see bb_debug_stall_attention).
+int flash_set_stall(int on);
 
 }  // namespace bb

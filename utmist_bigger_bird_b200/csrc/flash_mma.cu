@@ -380,6 +380,7 @@ int flash_check(const bb_flash_args* a) {
   if (a->d <= 0 || a->d > 128 || a->d % 8) return fail(BB_ERR_UNSUPPORTED, "flash: head_dim must be a multiple of 8 and <= 128");
   if (a->front < 0 || a->window < 1) return fail(BB_ERR_ARG, "front >= 0 and window >= 1 required");
   if (a->n < a->t) return fail(BB_ERR_SHAPE, "Key sequence must be at least as long as query sequence");
+  if (a->n > 0x7fffffffLL) return fail(BB_ERR_UNSUPPORTED, "flash: sequences longer than 2^31 - 1 keys are not supported");
   if (a->route_chunk <= 0 || a->route_groups < 1 || a->route_k < 0) return fail(BB_ERR_SHAPE, "flash: bad route groups");
   if (a->row_begin < 0 || a->row_end > a->t || a->row_begin > a->row_end) return fail(BB_ERR_ARG, "flash: bad row range");
   return BB_OK;
@@ -434,6 +435,7 @@ int flash(const bb_flash_args* a, void* ws, size_t ws_bytes, cudaStream_t stream
   p.scale_log2 = a->scale * LOG2E;
   p.splits = splits_of(a);
   p.bh = a->bh;
+  p.serial = 0;
   const int dp = dpad_of(a->d);
   char* w = static_cast<char*>(ws);
   p.part_acc = reinterpret_cast<float*>(w);

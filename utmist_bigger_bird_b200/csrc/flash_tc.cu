@@ -47,10 +47,9 @@ constexpr float RESCALE_LOG2 = 8.0f;
 
 constexpr uint32_t SM_Q = 0;
 constexpr uint32_t SM_KV = TILE;
-constexpr uint32_t SM_POS = SM_KV + NB * TILE;  // [2][128] int32 routed-tile positions
 enum { B_Q = 0, B_FULL = 1, B_EMPTY = B_FULL + NB, B_S = B_EMPTY + NB, B_P = B_S + 2, B_O = B_P + 2,
        B_DONE = B_O + 1, N_BARS = B_DONE + 1 };
-constexpr uint32_t SM_BAR = SM_POS + 2 * 128 * 4;
+constexpr uint32_t SM_BAR = SM_KV + NB * TILE;
 constexpr uint32_t SM_MISC = SM_BAR + N_BARS * 8;  // [0] TMEM base, [1] abort flag
 constexpr uint32_t SM_BYTES = SM_MISC + 16;
 constexpr uint32_t SM_ALLOC = SM_BYTES + 1024;     // slack to align the base to 1024 bytes
@@ -60,7 +59,11 @@ constexpr uint32_t COL_O = 256;
 
 // Fault codes written to this unit's fault word (which wait gave up).
 enum { F_SOFTMAX_S = 1, F_SOFTMAX_O = 2, F_MMA_Q = 3, F_MMA_K = 4, F_MMA_P = 5, F_MMA_V = 6,
-       F_PROD_EMPTY = 7, F_EPI_O = 8 };
+       F_PROD_EMPTY = 7, F_EPI_O = 8, F_MMA_STALL = 9 };
+
+// Test hook of the abort path (bb_debug_stall_attention): when non-zero, the MMA issuer of every
+// CTA first waits for a barrier that nothing completes, so its bounded wait runs out.
+static __device__ int g_tc_stall = 0;
 
 
 // ----------------------------------------------------------------------------- tile schedule
@@ -137,33 +140,28 @@ __device__ __forceinline__ int64_t routed_pos(const FlashParams& p, int64_t h, i
   return (ps < 0 || ps >= p.n) ? -1 : ps;
 }
 
-// Masks one row of a 128-key tile. Contiguous tiles (kind 0, first key k0): key k0 + i is valid
-// iff k0 + i <= q and (k0 + i < front or k0 + i >= q - W + 1). Routed tiles (kind 1): slot i's
-// key ps (-1 = empty) is valid iff front <= ps <= q - W and the row's route group is the tile's.
-// Bounds are folded into per-row int32 limits first (positions are < 2^31), so the per-element
-// work is two compares and a select. (Calls with a token mask run on the mma.sync kernel.)
-__device__ __forceinline__ void mask_row(float* s, int kind, int64_t k0, int64_t group, const FlashParams& p,
-                                         int64_t qpos, int64_t qgroup, const int32_t* ps_s, int64_t batch) {
-  if (kind == 0) {
-    const int hi = (int)max(min(qpos - k0, (int64_t)128), (int64_t)-1);
-    const int f = (int)max(min(p.front - k0, (int64_t)128), (int64_t)0);
-    const int lo = (int)max(min(qpos - p.window + 1 - k0, (int64_t)129), (int64_t)0);
+// Routed positions of one 128-slot tile, held by a warp: lane l keeps the positions of slots l,
+// l + 32, l + 64 and l + 96 (-1 = empty or out of range) and the mask reads slot i with a shuffle.
+// Each warp loads its own copy (the four warps of a softmax group read the same 512 bytes, L1
+// hits), so no barrier between warps is needed: a barrier there could strand the other warps of
+// the group when one warp leaves on an abort.
+struct RoutedPos {
+  int32_t v[4];
+};
+__device__ __forceinline__ RoutedPos load_routed(const FlashParams& p, int64_t h, int64_t group, int64_t slot0,
+                                                 int lane) {
+  RoutedPos r;
 #pragma unroll
-    for (int i = 0; i < 128; ++i)
-      if (!(i <= hi && (i < f || i >= lo))) s[i] = -INFINITY;
-  } else {
-    const int hr = qgroup == group ? (int)max(min(qpos - p.window, (int64_t)0x7fffffff), (int64_t)-1) : -1;
-    const int fr = (int)min(p.front, (int64_t)0x7fffffff);
-#pragma unroll
-    for (int i = 0; i < 128; ++i) {
-      const int ps = ps_s[i];
-      if (!(ps >= fr && ps <= hr)) s[i] = -INFINITY;
-    }
-  }
+  for (int k = 0; k < 4; ++k) r.v[k] = (int32_t)routed_pos(p, h, group, slot0 + lane + 32 * k);
+  return r;
 }
 
-// Per-row mask limits of a tile (see mask_row): contiguous tiles keep column i iff
-// i <= hi && (i < f || i >= lo); routed tiles keep slot i iff f <= ps_s[i] <= hi.
+// Per-row mask limits of a tile. Contiguous tiles (kind 0, first key k0): key k0 + i is valid iff
+// k0 + i <= q and (k0 + i < front or k0 + i >= q - W + 1), i.e. i <= hi && (i < f || i >= lo).
+// Routed tiles (kind 1): slot i's key ps (-1 = empty) is valid iff front <= ps <= q - W and the
+// row's route group is the tile's, i.e. f <= ps <= hi. Bounds are folded into per-row int32
+// limits first (positions are < 2^31), so the per-element work is two compares and a select.
+// (Calls with a token mask run on the mma.sync kernel.)
 struct MaskLimits {
   int hi, f, lo;
 };
@@ -181,23 +179,19 @@ __device__ __forceinline__ MaskLimits mask_limits(int kind, int64_t k0, int64_t 
   }
   return m;
 }
-// Masks columns base .. base+NC-1 of a row held in s[0..NC-1].
-template <int NC>
-__device__ __forceinline__ void mask_cols(float* s, int base, int kind, const MaskLimits& m, const int32_t* ps_s) {
+// Masks the 128 columns of a row held in s[0..127] (warp-uniform call: routed tiles shuffle).
+__device__ __forceinline__ void mask_cols128(float* s, int kind, const MaskLimits& m, const RoutedPos& rp) {
   if (kind == 0) {
 #pragma unroll
-    for (int i = 0; i < NC; ++i)
-      if (!(base + i <= m.hi && (base + i < m.f || base + i >= m.lo))) s[i] = -INFINITY;
+    for (int i = 0; i < 128; ++i)
+      if (!(i <= m.hi && (i < m.f || i >= m.lo))) s[i] = -INFINITY;
   } else {
 #pragma unroll
-    for (int i = 0; i < NC; ++i) {
-      const int ps = ps_s[base + i];
+    for (int i = 0; i < 128; ++i) {
+      const int ps = __shfl_sync(0xffffffffu, rp.v[i >> 5], i & 31);
       if (!(ps >= m.f && ps <= m.hi)) s[i] = -INFINITY;
     }
   }
-}
-__device__ __forceinline__ void mask_half(float* s, int half, int kind, const MaskLimits& m, const int32_t* ps_s) {
-  mask_cols<64>(s, 64 * half, kind, m, ps_s);
 }
 
 struct TcMaps {
@@ -212,8 +206,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
   const uint32_t sbase = (raw + 1023u) & ~1023u;
   unsigned char* sptr = smem_raw + (sbase - raw);
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(sptr + SM_MISC);
-  volatile uint32_t* abort_flag = misc + 1;
-  int32_t* pos_s = reinterpret_cast<int32_t*>(sptr + SM_POS);
+  const Abort abort_flag{misc + 1, p.serial};
   auto bar = [&](int i) { return sbase + SM_BAR + 8u * (uint32_t)i; };
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -328,6 +321,8 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
     if (nt > 0) {
       constexpr uint32_t ID_QK = idesc<T>(false), ID_PV = idesc<T>(true);
       bool ok = mbar_wait_warp(bar(B_Q), 0, abort_flag, F_MMA_Q);
+      // Test hook (bb_debug_stall_attention): see flash_tc_pair_kernel.
+      if (ok && *(volatile int*)&g_tc_stall) ok = mbar_wait_warp(bar(B_DONE), 0, abort_flag, F_MMA_STALL);
       auto issue_pv = [&](int i) -> bool {
         if (!mbar_wait_warp(bar(B_P + (i & 1)), (i >> 1) & 1, abort_flag, F_MMA_P)) return false;
         const int itv = 2 * i + 1, bv = itv % NB;
@@ -369,11 +364,8 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
       const Tile tl = tile_at(p, sc, t_begin + j);
-      int32_t* ps_s = pos_s + (j & 1) * 128;
-      if (tl.kind == 1) {
-        ps_s[row] = (int32_t)routed_pos(p, h, tl.group, tl.slot0 + row);
-        named_sync(1, 128);
-      }
+      const MaskLimits ml = tl.masked ? mask_limits(tl.kind, tl.k0, tl.group, p, qpos, qgroup)
+                                      : MaskLimits{127, 128, 0};
       if (!mbar_wait_warp(bar(B_S + (j & 1)), (j >> 1) & 1, abort_flag, F_SOFTMAX_S)) {
         ok = false;
         break;
@@ -382,7 +374,9 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
       float s[128];
       const uint32_t scol = tl_lane + (uint32_t)(j & 1) * 128u;
       tmem_ld128(scol, s);
-      if (tl.masked) mask_row(s, tl.kind, tl.k0, tl.group, p, qpos, qgroup, ps_s, batch);
+      if (tl.masked)
+        mask_cols128(s, tl.kind, ml, tl.kind == 1 ? load_routed(p, h, tl.group, tl.slot0, lane)
+                                                  : RoutedPos{{-1, -1, -1, -1}});
       // Row max as a tree (short dependency chains).
       float mx8[8];
 #pragma unroll
@@ -446,7 +440,6 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(B_P + (j & 1)));
-      if (tl.kind == 1) named_sync(1, 128);  // ps_s[(j & 1)] is rewritten two tiles later
     }
     // Epilogue: wait for the last P.V, normalise, store.
     bool have_o = false;
@@ -505,10 +498,11 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
 }
 
 // ============================================================================= paired kernel
-// Two query heads of one KV head (a GQA pair, heads 2m and 2m+1) x 128 query rows per CTA. The
-// K/V tiles of the sink and window are loaded once for both heads; the routed tiles of head A and
-// then of head B follow (each head masks the other head's routed tiles entirely and writes P = 0
-// for them). Each head has its own softmax warpgroup, S buffer and O accumulator in TMEM:
+// Two query heads of one KV head (a GQA pair, heads 2m and 2m+1) x 128 query rows per CTA. A step
+// is one 128-key tile per head: the K/V tiles of the sink and window are shared by both heads
+// and loaded once; in a routed step each head gets its own gathered K/V tile (its r-th routed
+// tile), so the tensor core never multiplies a head by keys it does not attend. Each head has its
+// own softmax warpgroup, S buffer and O accumulator in TMEM:
 //   S_A = columns 0-127, S_B = 128-255, O_A = 256-383, O_B = 384-511.
 // The single MMA thread alternates  P_A V -> S_A(next) -> P_B V -> S_B(next), so while one
 // warpgroup runs its softmax the tensor core works for the other (ping-pong).
@@ -517,51 +511,28 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
 // softmax of head A (warps 2-5) and of head B (warps 6-9); warp w reads TMEM lanes
 // 32 * (w % 4) .. 32 * (w % 4) + 31, so each softmax group covers all 128 rows.
 constexpr int P_THREADS = 320;
-// K/V ring: 5 slots of 32 KB (K_j, V_j alternate), the most that fits beside the two Q tiles in
-// 227 KB; the extra slot gives the TMA of the next tiles more lead over the MMA issuer.
+// K/V ring: 5 slots of 32 KB, the most that fits beside the two Q tiles in 227 KB. Fill order:
+// a shared step loads K_j then V_j (two fills), a routed step K_A, K_B, V_A, V_B (four fills). At
+// most four filled slots are in use at once (V_A, V_B of the previous step and K_A, K_B of this
+// one), so the fifth gives the loads of the next tiles lead over the MMA issuer.
 constexpr int PNB = 5;
 constexpr uint32_t P_SM_QA = 0;
 constexpr uint32_t P_SM_QB = TILE;
 constexpr uint32_t P_SM_KV = 2 * TILE;
-constexpr uint32_t P_SM_POS = P_SM_KV + PNB * TILE;  // [2 heads][128] int32 routed positions
 // PB_P + 2w: P_w columns for keys 0-63 stored, PB_P + 2w + 1: keys 64-127 stored.
 enum { PB_Q = 0, PB_FULL = 1, PB_EMPTY = PB_FULL + PNB, PB_S = PB_EMPTY + PNB, PB_P = PB_S + 2, PB_O = PB_P + 4,
        PB_DONE = PB_O + 2, PN_BARS = PB_DONE + 1 };
-constexpr uint32_t P_SM_BAR = P_SM_POS + 2 * 128 * 4;
+constexpr uint32_t P_SM_BAR = P_SM_KV + PNB * TILE;
 constexpr uint32_t P_SM_MISC = P_SM_BAR + PN_BARS * 8;
 constexpr uint32_t P_SM_ALLOC = P_SM_MISC + 16 + 1024;
 static_assert(P_SM_ALLOC <= 232448, "pair kernel shared memory exceeds the 227 KB per-block limit");
 
-struct Tile2 {
-  int kind;   // 0 contiguous (both heads), 1 routed
-  int owner;  // routed tiles: 0 = head A, 1 = head B
-  int64_t k0, group, slot0;
-  bool masked;
+// Ring fills of a split whose first `shared` steps are shared: step j < shared fills 2j (K) and
+// 2j + 1 (V); a routed step j fills F, F+1, F+2, F+3 = K_A, K_B, V_A, V_B with
+// F = 2 * shared + 4 * (j - shared). Fill f uses slot f % PNB in round f / PNB.
+struct PairFills {
+  int shared;
 };
-
-__device__ __forceinline__ Tile2 tile2_at(const FlashParams& p, const Sched& s, int t) {
-  Tile2 r;
-  if (t < s.n_contig) {
-    const Tile a = tile_at(p, s, t);
-    r.kind = 0;
-    r.owner = 0;
-    r.k0 = a.k0;
-    r.group = 0;
-    r.slot0 = 0;
-    r.masked = a.masked;
-  } else {
-    const int per_head = s.n_groups * s.n_rpg;
-    const int q = t - s.n_contig;
-    r.kind = 1;
-    r.owner = q / per_head;
-    const int rr = q % per_head;
-    r.k0 = 0;
-    r.group = s.g_lo + rr / s.n_rpg;
-    r.slot0 = (int64_t)(rr % s.n_rpg) * BN;
-    r.masked = true;
-  }
-  return r;
-}
 
 template <typename T>
 __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __grid_constant__ TcMaps maps,
@@ -571,8 +542,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
   const uint32_t sbase = (raw + 1023u) & ~1023u;
   unsigned char* sptr = smem_raw + (sbase - raw);
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(sptr + P_SM_MISC);
-  volatile uint32_t* abort_flag = misc + 1;
-  int32_t* pos_s = reinterpret_cast<int32_t*>(sptr + P_SM_POS);
+  const Abort abort_flag{misc + 1, p.serial};
   auto bar = [&](int i) { return sbase + P_SM_BAR + 8u * (uint32_t)i; };
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -581,10 +551,10 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
   const int64_t row0 = p.row_begin + (int64_t)blockIdx.x * BM;
   const int64_t row1 = min(row0 + BM, p.row_end);
   const int64_t kvh = (hA / p.num_heads) * (p.num_heads / p.kv_groups) + (hA % p.num_heads) / p.kv_groups;
-  Sched sc = make_sched(p, row0, row1);
-  sc.total = sc.n_contig + 2 * sc.n_groups * sc.n_rpg;
+  const Sched sc = make_sched(p, row0, row1);
   const int t_begin = (int)((int64_t)sc.total * split / p.splits);
   const int nt = (int)((int64_t)sc.total * (split + 1) / p.splits) - t_begin;
+  const PairFills fl{max(0, min(sc.n_contig - t_begin, nt))};
 
   if (threadIdx.x == 0) {
     mbar_init(bar(PB_Q), 1);
@@ -636,46 +606,83 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
         }
         const T* kbase = static_cast<const T*>(p.k) + kvh * p.sk_h;
         const T* vbase = static_cast<const T*>(p.v) + kvh * p.sv_h;
-        for (int it = 0; it < 2 * nt; ++it) {
-          const int j = it >> 1;
-          const bool is_v = it & 1;
-          const int b = it % PNB;
-          const int round = it / PNB;
-          if (round > 0 && !mbar_wait_warp(bar(PB_EMPTY + b), (round - 1) & 1, abort_flag, F_PROD_EMPTY)) break;
-          const Tile2 tl = tile2_at(p, sc, t_begin + j);
-          const uint32_t dst = sbase + P_SM_KV + (uint32_t)b * TILE;
-          if (tl.kind == 0) {
-            {
-              const CUtensorMap* m = is_v ? &maps.v : &maps.k;
-              const int c1 = (int)tl.k0, c2 = (int)kvh;
-              mbar_expect_tx_one(bar(PB_FULL + b), TILE);
-              if (maps.kv_swap) {
-                tma_load_3d_one(dst, m, 0, c2, c1, bar(PB_FULL + b));
-                tma_load_3d_one(dst + HALF, m, 64, c2, c1, bar(PB_FULL + b));
-              } else {
-                tma_load_3d_one(dst, m, 0, c1, c2, bar(PB_FULL + b));
-                tma_load_3d_one(dst + HALF, m, 64, c1, c2, bar(PB_FULL + b));
-              }
+        int it = 0;
+        bool ok = true;
+        // Shared steps: K_j then V_j, each a pair of tiled TMA loads.
+        for (int j = 0; ok && j < fl.shared; ++j) {
+          const Tile tl = tile_at(p, sc, t_begin + j);
+          for (int f = 0; f < 2; ++f, ++it) {
+            const int b = it % PNB;
+            const int round = it / PNB;
+            if (round > 0 && !mbar_wait_warp(bar(PB_EMPTY + b), (round - 1) & 1, abort_flag, F_PROD_EMPTY)) {
+              ok = false;
+              break;
             }
-          } else {
-            const T* src_base = is_v ? vbase : kbase;
-            const int64_t sstride = is_v ? p.sv_t : p.sk_t;
-            for (int r = lane; r < BN; r += 32) {
-              const int64_t ps = routed_pos(p, hA + tl.owner, tl.group, tl.slot0 + r);
-              const T* row = src_base + (ps < 0 ? 0 : ps) * sstride;
-#pragma unroll
-              for (int c = 0; c < 16; ++c) {
-                const uint32_t d = dst + (uint32_t)(c >> 3) * HALF + (uint32_t)r * 128u +
-                                   (uint32_t)(((c & 7) ^ (r & 7)) << 4);
-                cp_async_16(d, row + c * 8, ps >= 0);
-              }
+            const uint32_t dst = sbase + P_SM_KV + (uint32_t)b * TILE;
+            const CUtensorMap* m = f ? &maps.v : &maps.k;
+            const int c1 = (int)tl.k0, c2 = (int)kvh;
+            mbar_expect_tx_one(bar(PB_FULL + b), TILE);
+            if (maps.kv_swap) {
+              tma_load_3d_one(dst, m, 0, c2, c1, bar(PB_FULL + b));
+              tma_load_3d_one(dst + HALF, m, 64, c2, c1, bar(PB_FULL + b));
+            } else {
+              tma_load_3d_one(dst, m, 0, c1, c2, bar(PB_FULL + b));
+              tma_load_3d_one(dst + HALF, m, 64, c1, c2, bar(PB_FULL + b));
             }
-            asm volatile("cp.async.wait_all;" ::: "memory");
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-            mbar_arrive_one(bar(PB_FULL + b));
+            ++fills[b];
           }
-          ++fills[b];
+        }
+        // Routed steps: K_A, K_B, V_A, V_B, each 128 rows gathered with cp.async (16 chunks of 16
+        // bytes per row) into the 128B-swizzled layout. The copies complete asynchronously on the
+        // slot's full barrier (cp.async.mbarrier.arrive from every lane, then one regular arrive),
+        // so the warp goes on issuing the next gathers instead of waiting for each; the positions of
+        // the next step are loaded while this step's copies are in flight.
+        if (ok && fl.shared < nt) {
+          int32_t pos[2][4], nxt[2][4];
+          auto load_pos = [&](int j, int32_t (&dst)[2][4]) {
+            const Tile tl = tile_at(p, sc, t_begin + j);
+#pragma unroll
+            for (int w = 0; w < 2; ++w)
+#pragma unroll
+              for (int i = 0; i < 4; ++i) dst[w][i] = (int32_t)routed_pos(p, hA + w, tl.group, tl.slot0 + lane + 32 * i);
+          };
+          load_pos(fl.shared, pos);
+          for (int j = fl.shared; ok && j < nt; ++j) {
+            for (int f = 0; f < 4; ++f, ++it) {
+              const int b = it % PNB;
+              const int round = it / PNB;
+              if (round > 0 && !mbar_wait_warp(bar(PB_EMPTY + b), (round - 1) & 1, abort_flag, F_PROD_EMPTY)) {
+                ok = false;
+                break;
+              }
+              const uint32_t dst = sbase + P_SM_KV + (uint32_t)b * TILE;
+              const T* src_base = f >= 2 ? vbase : kbase;
+              const int64_t sstride = f >= 2 ? p.sv_t : p.sk_t;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int r = lane + 32 * i;
+                const int32_t ps = (f & 1) ? pos[1][i] : pos[0][i];
+                const T* row = src_base + (int64_t)(ps < 0 ? 0 : ps) * sstride;
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                  const uint32_t d = dst + (uint32_t)(c >> 3) * HALF + (uint32_t)r * 128u +
+                                     (uint32_t)(((c & 7) ^ (r & 7)) << 4);
+                  cp_async_16(d, row + c * 8, ps >= 0);
+                }
+              }
+              asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar(PB_FULL + b)) : "memory");
+              __syncwarp();
+              mbar_arrive_one(bar(PB_FULL + b));
+              ++fills[b];
+            }
+            if (ok && j + 1 < nt) {
+              load_pos(j + 1, nxt);
+#pragma unroll
+              for (int w = 0; w < 2; ++w)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) pos[w][i] = nxt[w][i];
+            }
+          }
         }
       }
       {
@@ -686,19 +693,24 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
     } else if (warp == 1 && nt > 0) {
       // ---------------------------------------------------------------- MMA issuer
       constexpr uint32_t ID_QK = idesc<T>(false), ID_PV = idesc<T>(true);
+      auto slot_of = [](int f) { return (uint32_t)(f % PNB); };
+      auto full_wait = [&](int f, int code) {
+        return mbar_wait_warp(bar(PB_FULL + f % PNB), (uint32_t)((f / PNB) & 1), abort_flag, code);
+      };
       auto s_mma = [&](int w, uint32_t kb) {
         const uint32_t qs = sbase + (w ? P_SM_QB : P_SM_QA);
         gemm_ss8(tmem + (uint32_t)w * 128u, desc_k(qs), desc_k(kb), ID_QK, 0u);
         mma_commit_one(bar(PB_S + w));
       };
-      // O_w += P_w(i) V_i in two K halves (keys 0-63, 64-127), each issued as soon as the softmax
-      // has stored that half of P; `wait_v`: the first of the two heads also waits for V_i.
-      auto pv = [&](int w, int i, bool wait_v) -> bool {
+      // O_w += P_w(i) V in two K halves (keys 0-63, 64-127), each issued as soon as the softmax has
+      // stored that half of P. `fv` is V's fill number; `wait_v`: wait for it (head A always, head B
+      // only for its own gathered V); `gathered`: cp.async-filled, fenced to the async proxy.
+      auto pv = [&](int w, int i, int fv, bool wait_v, bool gathered) -> bool {
         if (!mbar_wait_warp(bar(PB_P + 2 * w), i & 1, abort_flag, F_MMA_P)) return false;
-        const int itv = 2 * i + 1, bv = itv % PNB;
-        if (wait_v && !mbar_wait_warp(bar(PB_FULL + bv), (itv / PNB) & 1, abort_flag, F_MMA_V)) return false;
+        if (wait_v && !full_wait(fv, F_MMA_V)) return false;
+        if (gathered) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         tc_fence_after();
-        const uint32_t vb = sbase + P_SM_KV + (uint32_t)bv * TILE;
+        const uint32_t vb = sbase + P_SM_KV + slot_of(fv) * TILE;
         const uint32_t od = tmem + 256u + (uint32_t)w * 128u, pa = tmem + (uint32_t)w * 128u;
         gemm_ts4(od, pa, desc_mn(vb), ID_PV, i > 0 ? 1u : 0u);
         if (!mbar_wait_warp(bar(PB_P + 2 * w + 1), i & 1, abort_flag, F_MMA_P)) return false;
@@ -708,28 +720,77 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
         return true;
       };
       bool ok = mbar_wait_warp(bar(PB_Q), 0, abort_flag, F_MMA_Q);
-      for (int j = 0; ok && j < nt; ++j) {
-        const int itk = 2 * j, bk = itk % PNB;
-        if (!mbar_wait_warp(bar(PB_FULL + bk), (itk / PNB) & 1, abort_flag, F_MMA_K)) {
+      // Test hook (bb_debug_stall_attention): wait for the end-of-kernel barrier, which only this
+      // warp completes, so the bounded wait runs out and the launch takes its abort path.
+      if (ok && *(volatile int*)&g_tc_stall) ok = mbar_wait_warp(bar(PB_DONE), 0, abort_flag, F_MMA_STALL);
+      const int c = fl.shared;
+      int j = 0;
+      // Shared steps (kept as one short loop: its code is the hot path).
+      for (; ok && j < c; ++j) {
+        const int fk = 2 * j;
+        if (!full_wait(fk, F_MMA_K)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t kb = sbase + P_SM_KV + (uint32_t)bk * TILE;
+        const uint32_t kb = sbase + P_SM_KV + slot_of(fk) * TILE;
         if (j > 0) {
-          if (!(ok = pv(0, j - 1, true))) break;
+          if (!(ok = pv(0, j - 1, fk - 1, true, false))) break;
           s_mma(0, kb);
-          if (!(ok = pv(1, j - 1, false))) break;
-          mma_commit_one(bar(PB_EMPTY + (2 * (j - 1) + 1) % PNB));  // V_{j-1} consumed by both heads
+          if (!(ok = pv(1, j - 1, fk - 1, false, false))) break;
+          mma_commit_one(bar(PB_EMPTY + slot_of(fk - 1)));  // V_{j-1} consumed by both heads
           s_mma(1, kb);
         } else {
           s_mma(0, kb);
           s_mma(1, kb);
         }
-        mma_commit_one(bar(PB_EMPTY + bk));  // K_j consumed by both heads
+        mma_commit_one(bar(PB_EMPTY + slot_of(fk)));  // K_j consumed by both heads
       }
-      if (ok && pv(0, nt - 1, true) && pv(1, nt - 1, false))
-        mma_commit_one(bar(PB_EMPTY + (2 * (nt - 1) + 1) % PNB));
+      // Routed steps: each head its own K and V (fills F, F+1, F+2, F+3 = K_A, K_B, V_A, V_B).
+      for (; ok && j < nt; ++j) {
+        const int F = 2 * c + 4 * (j - c);
+        if (!full_wait(F, F_MMA_K)) {
+          ok = false;
+          break;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tc_fence_after();
+        if (j > 0) {
+          const bool prev_routed = j - 1 >= c;
+          const int fva = prev_routed ? F - 2 : F - 1, fvb = F - 1;
+          if (!(ok = pv(0, j - 1, fva, true, prev_routed))) break;
+          if (prev_routed) mma_commit_one(bar(PB_EMPTY + slot_of(fva)));
+          s_mma(0, sbase + P_SM_KV + slot_of(F) * TILE);
+          mma_commit_one(bar(PB_EMPTY + slot_of(F)));
+          if (!(ok = pv(1, j - 1, fvb, prev_routed, prev_routed))) break;
+          mma_commit_one(bar(PB_EMPTY + slot_of(fvb)));
+        } else {
+          s_mma(0, sbase + P_SM_KV + slot_of(F) * TILE);
+          mma_commit_one(bar(PB_EMPTY + slot_of(F)));
+        }
+        if (!full_wait(F + 1, F_MMA_K)) {
+          ok = false;
+          break;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tc_fence_after();
+        s_mma(1, sbase + P_SM_KV + slot_of(F + 1) * TILE);
+        mma_commit_one(bar(PB_EMPTY + slot_of(F + 1)));
+      }
+      if (ok) {
+        const int last = nt - 1;
+        if (last < c) {
+          const int fv = 2 * last + 1;
+          if (pv(0, last, fv, true, false) && pv(1, last, fv, false, false))
+            mma_commit_one(bar(PB_EMPTY + slot_of(fv)));
+        } else {
+          const int F = 2 * c + 4 * (last - c);
+          if (pv(0, last, F + 2, true, true)) {
+            mma_commit_one(bar(PB_EMPTY + slot_of(F + 2)));
+            if (pv(1, last, F + 3, true, true)) mma_commit_one(bar(PB_EMPTY + slot_of(F + 3)));
+          }
+        }
+      }
       mma_commit_one(bar(PB_DONE));
       mbar_drain(bar(PB_DONE), 0);
     }
@@ -745,17 +806,13 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
     const uint32_t ocol = tl_lane + 256u + (uint32_t)w * 128u;
     const int64_t qpos = p.offset + row0 + row;
     const int64_t qgroup = qpos / p.route_chunk;
-    int32_t* ps_s = pos_s + w * 128;
     const float c = p.scale_log2;
     float m_ref = -1.0e20f, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
-      const Tile2 tl = tile2_at(p, sc, t_begin + j);
-      const bool own = tl.kind == 0 || tl.owner == w;
-      if (own && tl.kind == 1) {
-        ps_s[row] = (int32_t)routed_pos(p, h, tl.group, tl.slot0 + row);
-        named_sync(1 + w, 128);
-      }
+      const Tile tl = tile_at(p, sc, t_begin + j);
+      const MaskLimits ml = tl.masked ? mask_limits(tl.kind, tl.k0, tl.group, p, qpos, qgroup)
+                                      : MaskLimits{127, 128, 0};
       if (!mbar_wait_warp(bar(PB_S + w), j & 1, abort_flag, F_SOFTMAX_S)) {
         ok = false;
         break;
@@ -767,86 +824,75 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
         break;
       }
       tc_fence_after();
-      bool lo_done = false;
-      if (own) {
-        // The whole S row in registers (one TMEM load), its exact max, then P = exp2(s * c - m_ref)
-        // written as packed 16-bit pairs over S columns [0, 64) in four 16-column stores.
-        const MaskLimits ml = tl.masked ? mask_limits(tl.kind, tl.k0, tl.group, p, qpos, qgroup)
-                                        : MaskLimits{127, 128, 0};
-        float s[128];
-        tmem_ld128(scol, s);
-        if (tl.masked) mask_cols<128>(s, 0, tl.kind, ml, ps_s);
-        float mx8[8];
+      // The whole S row in registers (one TMEM load), its exact max, then P = exp2(s * c - m_ref)
+      // written as packed 16-bit pairs over S columns [0, 64) in four 16-column stores.
+      float s[128];
+      tmem_ld128(scol, s);
+      if (tl.masked)
+        mask_cols128(s, tl.kind, ml, tl.kind == 1 ? load_routed(p, h, tl.group, tl.slot0, lane)
+                                                  : RoutedPos{{-1, -1, -1, -1}});
+      float mx8[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(s[k], s[8 + k]);
+      for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(s[k], s[8 + k]);
 #pragma unroll
-        for (int i = 16; i < 128; i += 16)
+      for (int i = 16; i < 128; i += 16)
 #pragma unroll
-          for (int k = 0; k < 8; ++k) mx8[k] = fmax3(mx8[k], s[i + k], s[i + 8 + k]);
-        const float mx = fmaxf(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], fmax3(mx8[5], mx8[6], mx8[7])));
-        const float mt = mx * c;
-        // Lazy rescale: the reference max moves only when the tile max passes it by more than
-        // 2^RESCALE_LOG2, so P stays below 2^RESCALE_LOG2 and most tiles leave O untouched.
-        float alpha = 1.f;
-        bool rescale_o = false;
-        if (mt > m_ref + RESCALE_LOG2) {
-          alpha = fast_exp2(m_ref - mt);
-          rescale_o = j > 0 && m_ref > -1.0e20f;
-          l *= alpha;
-          m_ref = mt;
-        }
-        // The O rescale uses warp-wide TMEM loads/stores, so it is decided per warp: lanes that
-        // keep their reference multiply by exactly 1. A warp that rescales holds back its
-        // first-half arrive until O is rescaled (the first P.V half accumulates into O).
-        if (!rescale_o) alpha = 1.f;
-        const bool warp_rescale = __any_sync(0xffffffffu, rescale_o);
-        float ls[4] = {0.f, 0.f, 0.f, 0.f};
-        const float neg = -m_ref;
-        const uint64_t c2 = f2_pack(c, c), n2 = f2_pack(neg, neg);
+        for (int k = 0; k < 8; ++k) mx8[k] = fmax3(mx8[k], s[i + k], s[i + 8 + k]);
+      const float mx = fmaxf(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], fmax3(mx8[5], mx8[6], mx8[7])));
+      const float mt = mx * c;
+      // Lazy rescale: the reference max moves only when the tile max passes it by more than
+      // 2^RESCALE_LOG2, so P stays below 2^RESCALE_LOG2 and most tiles leave O untouched.
+      float alpha = 1.f;
+      bool rescale_o = false;
+      if (mt > m_ref + RESCALE_LOG2) {
+        alpha = fast_exp2(m_ref - mt);
+        rescale_o = j > 0 && m_ref > -1.0e20f;
+        l *= alpha;
+        m_ref = mt;
+      }
+      // The O rescale uses warp-wide TMEM loads/stores, so it is decided per warp: lanes that
+      // keep their reference multiply by exactly 1. A warp that rescales holds back its
+      // first-half arrive until O is rescaled (the first P.V half accumulates into O).
+      if (!rescale_o) alpha = 1.f;
+      const bool warp_rescale = __any_sync(0xffffffffu, rescale_o);
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      const float neg = -m_ref;
+      const uint64_t c2 = f2_pack(c, c), n2 = f2_pack(neg, neg);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float xa, xb;
-            f2_unpack(f2_fma(f2_pack(s[32 * q + 2 * i], s[32 * q + 2 * i + 1]), c2, n2), xa, xb);
-            const float a = fast_exp2(xa), b = fast_exp2(xb);
-            ls[i & 3] += a + b;
-            pk[i] = pack2<T>(a, b);
-          }
-          tmem_st16(scol + 16u * q, pk);
-          if (q == 1 && !warp_rescale) {
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(bar(PB_P + 2 * w));
-          }
-        }
-        lo_done = !warp_rescale;
-        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-        // O(j-1) is complete (waited above) and no part of P(j).V(j) is issued before this warp's
-        // first-half arrive below.
-        if (warp_rescale) {
-#pragma unroll 1
-          for (int q4 = 0; q4 < 4; ++q4) {
-            float o[32];
-            tmem_ld32(ocol + q4 * 32, o);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(ocol + q4 * 32, o);
-          }
-        }
-      } else {
+      for (int q = 0; q < 4; ++q) {
         uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = 0u;
+        for (int i = 0; i < 16; ++i) {
+          float xa, xb;
+          f2_unpack(f2_fma(f2_pack(s[32 * q + 2 * i], s[32 * q + 2 * i + 1]), c2, n2), xa, xb);
+          const float a = fast_exp2(xa), b = fast_exp2(xb);
+          ls[i & 3] += a + b;
+          pk[i] = pack2<T>(a, b);
+        }
+        tmem_st16(scol + 16u * q, pk);
+        if (q == 1 && !warp_rescale) {
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(bar(PB_P + 2 * w));
+        }
+      }
+      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      // O(j-1) is complete (waited above) and no part of P(j).V(j) is issued before this warp's
+      // first-half arrive below.
+      if (warp_rescale) {
+#pragma unroll 1
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float o[32];
+          tmem_ld32(ocol + q4 * 32, o);
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) tmem_st16(scol + 16u * q4, pk);
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(ocol + q4 * 32, o);
+        }
       }
       tmem_wait_st();
       tc_fence_before();
-      if (!lo_done) mbar_arrive(bar(PB_P + 2 * w));
+      if (warp_rescale) mbar_arrive(bar(PB_P + 2 * w));
       mbar_arrive(bar(PB_P + 2 * w + 1));
-      if (own && tl.kind == 1) named_sync(1 + w, 128);
     }
     bool have_o = false;
     if (ok && nt > 0) have_o = mbar_wait_warp(bar(PB_O + w), (nt - 1) & 1, abort_flag, F_EPI_O);
@@ -980,6 +1026,7 @@ int make_map(CUtensorMap* m, int* swap, const void* base, int dtype, int64_t hea
 
 template <typename T>
 int launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream) {
+  p.serial = unit_next_serial();
   TcMaps maps;
   const int64_t hk = a->bh / a->kv_groups;
   int st = make_map(&maps.q, &maps.q_swap, a->q, a->dtype, a->bh, a->t, a->sq_h, a->sq_t);
@@ -1017,7 +1064,7 @@ int flash_tc_splits(const bb_flash_args* a, int sms) {
   const bool pair = tc::pair_mode(a);
   const int64_t ctas = cdiv(rows, tc::BM) * (pair ? a->bh / 2 : a->bh);
   const int64_t tiles = cdiv(std::min(a->n, a->window + tc::BM), tc::BN) + cdiv(a->front, tc::BN) +
-                        (pair ? 2 : 1) * cdiv(a->route_k, tc::BN);
+                        cdiv(a->route_k, tc::BN);
   if (ctas <= 0 || ctas >= 2LL * sms || tiles < 16) return 1;
   int best = 1;
   int64_t best_cost = cdiv(ctas, sms) * tiles;
@@ -1034,6 +1081,13 @@ int flash_tc_splits(const bb_flash_args* a, int sms) {
 int flash_tc_launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream) {
   if (a->dtype == BB_BF16) return tc::launch<__nv_bfloat16>(a, p, stream);
   return tc::launch<__half>(a, p, stream);
+}
+
+int flash_set_wait_limit(unsigned long long ns) { return tc::unit_set_wait_limit(ns); }
+
+int flash_set_stall(int on) {
+  const int v = on ? 1 : 0;
+  return cudaMemcpyToSymbol(tc::g_tc_stall, &v, sizeof(int)) == cudaSuccess ? 0 : -1;
 }
 
 int flash_fault_take(int* code) {

@@ -90,7 +90,7 @@ __device__ __forceinline__ void load_rows(const RtTcArgs& a, uint32_t qs, int64_
 
 // Producer: the CTA's K tiles [t0, t1) of KV head kv into the ring (TMA, zero fill past n).
 __device__ __forceinline__ void produce_k(const CUtensorMap* kmap, int kswap, int64_t kv, int64_t t0, int nt,
-                                          uint32_t sbase, volatile uint32_t* abort_flag, uint32_t bars) {
+                                          uint32_t sbase, Abort abort_flag, uint32_t bars) {
   auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
   int fills[NB];
 #pragma unroll
@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(THREADS, 1) rt_stats_kernel(const __grid_const
   const uint32_t sbase = (raw + 1023u) & ~1023u;
   unsigned char* sptr = smem_raw + (sbase - raw);
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(sptr + SM_MISC);
-  volatile uint32_t* abort_flag = misc + 1;
+  const Abort abort_flag{misc + 1, 0u};
   int64_t* rowpos = reinterpret_cast<int64_t*>(sptr + SM_ROWPOS);
   const uint32_t bars = sbase + SM_BAR;
   auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(THREADS, 1) rt_col_kernel(const __grid_constan
   const uint32_t sbase = (raw + 1023u) & ~1023u;
   unsigned char* sptr = smem_raw + (sbase - raw);
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(sptr + SM_MISC);
-  volatile uint32_t* abort_flag = misc + 1;
+  const Abort abort_flag{misc + 1, 0u};
   int64_t* rowpos = reinterpret_cast<int64_t*>(sptr + SM_ROWPOS);
   float* rowbias = reinterpret_cast<float*>(sptr + SM_ROWSTAT);
   const uint32_t bars = sbase + SM_BAR;
@@ -464,6 +464,8 @@ int routes_tc_col(const RtTcArgs& a, cudaStream_t stream) {
   return a.dtype == BB_BF16 ? rtc::launch_col<__nv_bfloat16>(a, m, swap, stream)
                             : rtc::launch_col<__half>(a, m, swap, stream);
 }
+
+int routes_set_wait_limit(unsigned long long ns) { return tc::unit_set_wait_limit(ns); }
 
 int routes_fault_take(int* code) {
   int v = 0;

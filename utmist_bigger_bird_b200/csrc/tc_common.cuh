@@ -7,6 +7,8 @@
 #pragma once
 #include <cudaTypedefs.h>
 
+#include <atomic>
+
 #include "bb_common.cuh"
 
 namespace bb {
@@ -18,6 +20,19 @@ constexpr uint32_t HALF = 16384u;  // 128 rows x 64 columns (one 128-byte swizzl
 // Fault word of the kernels in the including translation unit (0 = no fault): the code of the
 // first bounded wait that gave up. Read and cleared by that unit's host side.
 static __device__ int g_tc_fault = 0;
+// Serial number of the latest launch of this unit in which a CTA gave up a wait (0 = none). The
+// other CTAs of that launch read it while they spin and leave at once: without it every CTA of a
+// grid would wait out its own limit, and a launch of many waves would take waves x the limit.
+static __device__ unsigned int g_tc_abort = 0;
+// Limit of one bounded wait in nanoseconds (bb_set_wait_limit_ns; 2 s by default).
+static __device__ unsigned long long g_tc_wait_ns = 2000000000ull;
+
+// The abort state a bounded wait consults: the CTA's shared-memory abort flag and the launch's
+// serial number (0: the launch does not take part in cross-CTA aborts).
+struct Abort {
+  volatile uint32_t* flag;
+  uint32_t serial;
+};
 
 // ----------------------------------------------------------------------------- PTX wrappers
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -43,13 +58,16 @@ __device__ __forceinline__ uint64_t gtimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
+// Limit of the drain waits on the way out (fixed: they wait only for copies and MMAs already
+// issued, which complete on their own).
+constexpr uint64_t DRAIN_LIMIT_NS = 2000000000ull;
 
-// Waits for the phase of `parity`: false if another role aborted or ~2 s passed (then it aborts).
+// Waits for the phase of `parity`: false if another role of this CTA, or another CTA of this
+// launch, aborted, or if the wait limit passed (then it aborts: flag, fault code, launch serial).
 // Fully inline (a call here costs the hand-offs on the critical path measurably): one
 // non-blocking test for the common already-completed case, then a try_wait spin that looks at
-// the abort flag and the clock every 64 polls.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag, int code) {
+// the abort state and the clock every 64 polls.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, Abort ab, int code) {
   uint32_t ok;
   asm volatile(
       "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
@@ -57,14 +75,22 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
       : "r"(bar), "r"(parity)
       : "memory");
   if (ok) return true;
+  // The global words (abort serial, limit) are read only on the every-64-polls check: a load left
+  // in flight when the wait succeeds would stall the next write of its register on the hand-off
+  // path between the warps.
   const uint64_t t0 = gtimer();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try(bar, parity)) return true;
     if ((it & 63) == 0) {
-      if (*abort_flag) return false;
-      if (gtimer() - t0 > WAIT_LIMIT_NS) {
-        *abort_flag = 1;
-        atomicExch(&g_tc_fault, code);
+      if (*ab.flag) return false;
+      if (ab.serial != 0 && *(volatile unsigned int*)&g_tc_abort == ab.serial) {
+        *ab.flag = 1;
+        return false;
+      }
+      if (gtimer() - t0 > *(volatile unsigned long long*)&g_tc_wait_ns) {
+        *ab.flag = 1;
+        atomicCAS(&g_tc_fault, 0, code);  // the first wait that gave up keeps its code
+        if (ab.serial != 0) atomicExch(&g_tc_abort, ab.serial);
         return false;
       }
     }
@@ -73,16 +99,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 // mbar_wait made warp-uniform (false if any lane gave up): every lane polls, and the warp stays
 // converged for the elect.sync issue or the warp-wide (.sync.aligned) TMEM accesses that follow,
 // and leaves together on an abort.
-__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
-                                               int code) {
-  const bool ok = mbar_wait(bar, parity, abort_flag, code);
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, Abort ab, int code) {
+  const bool ok = mbar_wait(bar, parity, ab, code);
   return __all_sync(0xffffffffu, ok);
 }
 // Bounded wait used while draining on the way out (ignores the abort flag).
 static __device__ __noinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
   const uint64_t t0 = gtimer();
   while (!mbar_try(bar, parity))
-    if (gtimer() - t0 > WAIT_LIMIT_NS) return;
+    if (gtimer() - t0 > DRAIN_LIMIT_NS) return;
 }
 
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
@@ -307,6 +332,18 @@ __device__ __forceinline__ void named_sync(int id, int count) {
 }
 
 // ----------------------------------------------------------------------------- host side
+// Per-unit control of the wait state above (each translation unit that includes this header has
+// its own copies; these helpers act on the including unit's symbols, on the current device).
+static inline int unit_set_wait_limit(unsigned long long ns) {
+  return cudaMemcpyToSymbol(g_tc_wait_ns, &ns, sizeof(ns)) == cudaSuccess ? 0 : -1;
+}
+// Next launch serial of the including unit (never 0).
+static inline uint32_t unit_next_serial() {
+  static std::atomic<uint32_t> serial{0};
+  uint32_t s = serial.fetch_add(1, std::memory_order_relaxed) + 1;
+  if (s == 0) s = serial.fetch_add(1, std::memory_order_relaxed) + 1;
+  return s;
+}
 // cuTensorMapEncodeTiled through the runtime's driver entry point (nullptr if unavailable).
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn();
 // 3-D TMA map over a [heads][rows][128] 16-bit view with element strides (s_head, s_row), box

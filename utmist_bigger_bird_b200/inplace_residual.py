@@ -1,13 +1,14 @@
-"""In-place residual adds in the Llama decoder layers (drop-in for
-``modal_rd/inplace_residual.py``; an exact memory saver for long prefill).
+"""Drop-in for ``modal_rd/inplace_residual.py``: Llama decoder layers whose two residual adds
+write into the layer's input tensor.
 
-HF's decoder layer computes ``residual + attn_out`` and ``residual + mlp_out`` into new [n, hidden]
-tensors while its input is still referenced (and the model keeps ``inputs_embeds`` alive for the
-whole layer loop). Adding in place into the layer's input makes the embedding output the one
-residual-stream buffer of every layer: two [n, hidden] tensors fewer at the prefill peak
-(~1 GB each at 128K tokens of a 4096-wide model). The adds are the same ops, so results are
-bit-identical. The layer's input tensor is modified: do not pass ``inputs_embeds`` that are still
-needed, or ask for ``output_hidden_states`` (they would alias). Inference only.
+What it saves: during a long prefill the stock layer allocates a fresh [n, hidden] tensor for each
+residual sum; writing the sums into the incoming hidden states instead keeps one residual buffer
+for the whole stack (about 1 GB per avoided tensor at 128K tokens and hidden size 4096). The two
+additions are the same torch ops in the same order, so outputs do not change by a bit.
+
+Caveat: the tensor passed into the first layer is overwritten. Callers must not reuse
+``inputs_embeds`` afterwards or request ``output_hidden_states`` (the saved states would all be
+the same storage). For inference only.
 """
 from __future__ import annotations
 
