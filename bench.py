@@ -43,8 +43,8 @@ KERNEL_SOURCES = [ROOT / "utmist_bigger_bird_b200" / "csrc" / f for f in ("flash
 # dram__bytes_write.sum) of config 2's main pass, and the hash of the kernel sources it was taken
 # on. When the sources change the figure no longer describes the kernel and the bench reports null.
 MAIN_TRAFFIC = {"sources_sha256": "9df179c55d4e9264", "bytes_per_launch": 636.41e6 * (131072 - 256) / (32768 - 256),
-                "capture": "32K window-16384 launch, 636.4 MB read+write, scaled by main-pass query rows x4.024; "
-                           "profiles/flash_tc_pair_main32k.md"}
+                "capture": "dram__bytes_read.sum + dram__bytes_write.sum of a 32K window-16384 launch (636.4 MB), "
+                           "scaled by main-pass query rows x4.024"}
 
 
 def sources_sha256():
