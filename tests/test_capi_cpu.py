@@ -191,3 +191,34 @@ def test_wait_limit_must_be_positive():
     L = _lib.lib()
     assert L.bb_set_wait_limit_ns(0) == _lib.BB_ERR_ARG
     assert "positive" in L.bb_last_error().decode()
+
+
+def test_routes_workspace_holds_long_row_topk_scratch():
+    """Rows longer than one cluster's shared memory (1M keys) select in two levels: the routing
+    workspace grows by the candidate buffers (32 segments x budget positions and values per row,
+    plus the second level's picks); at 128K there is no such scratch."""
+    L = _lib.lib()
+
+    def ws(n):
+        a = _lib.RoutesArgs(heads=32, kv_heads=8, n=n, d=128, r=64, sink=64, window=16384, budget=512,
+                            scaling=0.088, dtype=_lib.BB_BF16)
+        nbytes = C.c_size_t(0)
+        assert L.bb_routes_workspace_size(C.byref(a), C.byref(nbytes)) == 0
+        return nbytes.value
+
+    def al(x):
+        return (x + 255) // 256 * 256
+
+    n = 1 << 20
+    col = al(32 * n * 4)
+    cand = al(32 * (n // 32768) * 512 * 4)
+    assert ws(n) - ws(n // 2 + 1) > col // 2            # the column scores grow with n
+    a = _lib.RoutesArgs(heads=32, kv_heads=8, n=n, d=128, r=64, sink=64, window=16384, budget=0,
+                        scaling=0.088, dtype=_lib.BB_BF16)
+    no_topk = C.c_size_t(0)
+    assert L.bb_routes_workspace_size(C.byref(a), C.byref(no_topk)) == 0
+    assert ws(n) - no_topk.value == 2 * cand + al(32 * 512 * 4)
+    a.n = 131072
+    small = C.c_size_t(0)
+    assert L.bb_routes_workspace_size(C.byref(a), C.byref(small)) == 0
+    assert ws(131072) == small.value

@@ -29,7 +29,8 @@
 namespace bb {
 
 int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, void* out, bool out64, int64_t so_h,
-                cudaStream_t stream);
+                void* scratch, size_t scratch_bytes, cudaStream_t stream);
+size_t topk_scratch_bytes(int64_t rows, int64_t n, int64_t k);
 
 namespace {
 
@@ -1196,7 +1197,7 @@ int launch_decode(const bb_decode_args* a, const DecodePlan& pl, char* ws, cudaS
 
 struct DroutePlan {
   int64_t splits, split_len;
-  size_t scores_bytes, m_bytes, l_bytes, probs_bytes, total;
+  size_t scores_bytes, m_bytes, l_bytes, probs_bytes, topk_bytes, total;
 };
 
 int plan_droute(const bb_decode_args* a, DroutePlan* pl) {
@@ -1216,7 +1217,8 @@ int plan_droute(const bb_decode_args* a, DroutePlan* pl) {
   pl->m_bytes = align_up(parts * 4, 256);
   pl->l_bytes = align_up(parts * 4, 256);
   pl->probs_bytes = a->out_probs ? 0 : align_up((size_t)a->kv_heads * a->cap * 4, 256);
-  pl->total = pl->scores_bytes + pl->m_bytes + pl->l_bytes + pl->probs_bytes;
+  pl->topk_bytes = align_up(topk_scratch_bytes(a->kv_heads, a->cap, a->route_k), 256);
+  pl->total = pl->scores_bytes + pl->m_bytes + pl->l_bytes + pl->probs_bytes + pl->topk_bytes;
   return BB_OK;
 }
 
@@ -1247,7 +1249,8 @@ int launch_droute(const bb_decode_args* a, const DroutePlan& pl, char* ws, cudaS
   droute_pool_kernel<<<dim3((unsigned)a->kv_heads, (unsigned)cdiv(a->cap, (int64_t)1024)), 256, 0, stream>>>(p);
   BB_CHECK_LAUNCH("droute_pool_kernel");
   if (a->route_k > 0 && a->out_idx) {
-    int st = topk_sorted(p.probs, a->kv_heads, a->cap, a->route_k, a->out_idx, a->out_idx_i64 != 0, a->so_i, stream);
+    int st = topk_sorted(p.probs, a->kv_heads, a->cap, a->route_k, a->out_idx, a->out_idx_i64 != 0, a->so_i,
+                         ws + pl.scores_bytes + pl.m_bytes + pl.l_bytes + pl.probs_bytes, pl.topk_bytes, stream);
     if (st) return st;
   }
   return BB_OK;

@@ -19,7 +19,8 @@
 namespace bb {
 
 int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, void* out, bool out64, int64_t so_h,
-                cudaStream_t stream);
+                void* scratch, size_t scratch_bytes, cudaStream_t stream);
+size_t topk_scratch_bytes(int64_t rows, int64_t n, int64_t k);
 
 namespace {
 
@@ -113,7 +114,7 @@ __global__ void evict_gather_kernel(EvictParams p, const char* __restrict__ k, i
 }
 
 struct EvictPlan {
-  size_t member_bytes, score_bytes, prio_bytes, sel_bytes, total;
+  size_t member_bytes, score_bytes, prio_bytes, sel_bytes, topk_bytes, total;
 };
 
 int esize(int dtype) { return dtype == BB_F32 ? 4 : 2; }
@@ -137,7 +138,8 @@ int plan_evict(const bb_evict_args* a, EvictPlan* pl) {
   pl->score_bytes = align_up(cells * sizeof(float), 256);
   pl->prio_bytes = align_up(cells * sizeof(float), 256);
   pl->sel_bytes = align_up((size_t)a->kv_heads * std::max<int64_t>(a->keep, 1) * sizeof(int32_t), 256);
-  pl->total = pl->member_bytes + pl->score_bytes + pl->prio_bytes + pl->sel_bytes;
+  pl->topk_bytes = align_up(topk_scratch_bytes(a->kv_heads, a->n, a->keep), 256);
+  pl->total = pl->member_bytes + pl->score_bytes + pl->prio_bytes + pl->sel_bytes + pl->topk_bytes;
   return BB_OK;
 }
 
@@ -192,7 +194,8 @@ int kv_evict(const bb_evict_args* a, void* ws, size_t ws_bytes, cudaStream_t str
     BB_CHECK_LAUNCH("evict_prio_direct_kernel");
   }
   if (a->keep > 0) {
-    st = topk_sorted(p.prio, a->kv_heads, a->n, a->keep, p.sel, false, a->keep, stream);
+    st = topk_sorted(p.prio, a->kv_heads, a->n, a->keep, p.sel, false, a->keep,
+                     w + pl.member_bytes + pl.score_bytes + pl.prio_bytes + pl.sel_bytes, pl.topk_bytes, stream);
     if (st) return st;
   }
   const int64_t L = a->sink + a->keep + a->window;

@@ -24,7 +24,8 @@
 namespace bb {
 
 int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, void* out, bool out64, int64_t so_h,
-                cudaStream_t stream);
+                void* scratch, size_t scratch_bytes, cudaStream_t stream);
+size_t topk_scratch_bytes(int64_t rows, int64_t n, int64_t k);
 namespace {
 
 constexpr int RT_THREADS = 256;   // 8 warps
@@ -522,6 +523,7 @@ struct RtPlan {
   int64_t r_pad, heads_per_block, row_blocks, chunks, groups;
   bool tc;                                        // tcgen05 score passes (routes_tc.cu)
   size_t partial_bytes, stats_bytes, col_bytes;   // stats_bytes = partials + merged rows
+  size_t topk_bytes;                              // long-row top-k scratch (after the column scores)
 };
 
 int plan_routes(const bb_routes_args* a, RtPlan* pl) {
@@ -549,6 +551,7 @@ int plan_routes(const bb_routes_args* a, RtPlan* pl) {
   pl->partial_bytes = align_up((size_t)a->kv_heads * pl->row_blocks * RT_ROWS * pl->chunks * sizeof(float2), 256);
   pl->stats_bytes = pl->partial_bytes + align_up((size_t)a->kv_heads * pl->row_blocks * RT_ROWS * sizeof(float2), 256);
   pl->col_bytes = a->out_col ? 0 : align_up((size_t)a->heads * a->n * sizeof(float), 256);
+  pl->topk_bytes = align_up(topk_scratch_bytes(a->heads, a->n, a->budget), 256);
   return BB_OK;
 }
 
@@ -597,7 +600,9 @@ int launch_routes_t(const bb_routes_args* a, const RtPlan& pl, char* ws, cudaStr
     route_col_kernel<T, DP><<<grid, RT_THREADS, smem, stream>>>(p);
     BB_CHECK_LAUNCH("route_col_kernel");
   }
-  if (a->budget > 0) return topk_sorted(p.col, a->heads, a->n, a->budget, a->out_idx, false, a->so_h, stream);
+  if (a->budget > 0)
+    return topk_sorted(p.col, a->heads, a->n, a->budget, a->out_idx, false, a->so_h,
+                       ws + pl.stats_bytes + pl.col_bytes, pl.topk_bytes, stream);
   return BB_OK;
 }
 
@@ -627,7 +632,7 @@ int routes_workspace_size(const bb_routes_args* a, size_t* bytes) {
   RtPlan pl;
   int st = plan_routes(a, &pl);
   if (st) return st;
-  *bytes = pl.stats_bytes + pl.col_bytes;
+  *bytes = pl.stats_bytes + pl.col_bytes + pl.topk_bytes;
   return BB_OK;
 }
 
@@ -635,9 +640,9 @@ int routes(const bb_routes_args* a, void* ws, size_t ws_bytes, cudaStream_t stre
   RtPlan pl;
   int st = plan_routes(a, &pl);
   if (st) return st;
-  if (ws_bytes < pl.stats_bytes + pl.col_bytes || (!ws && pl.stats_bytes + pl.col_bytes))
-    return fail(BB_ERR_WORKSPACE, "routes: workspace too small (%zu < %zu)", ws_bytes,
-                pl.stats_bytes + pl.col_bytes);
+  const size_t need = pl.stats_bytes + pl.col_bytes + pl.topk_bytes;
+  if (ws_bytes < need || (!ws && need))
+    return fail(BB_ERR_WORKSPACE, "routes: workspace too small (%zu < %zu)", ws_bytes, need);
   if (!a->q || !a->k || !a->qpos || (a->budget > 0 && !a->out_idx)) return fail(BB_ERR_ARG, "routes: null pointer");
   if (!aligned16(a->q) || !aligned16(a->k) || (a->sq_h * 2) % 16 || (a->sq_t * 2) % 16 ||
       (a->sk_h * 2) % 16 || (a->sk_t * 2) % 16)

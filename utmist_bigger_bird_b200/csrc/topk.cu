@@ -18,8 +18,14 @@
 //            offsets from a cluster-wide exclusive sum of the per-CTA counts, thread offsets from
 //            block scans
 //
-// The result is bit-identical to the single-CTA kernel (same order keys, same tie rule); rows
-// whose segments do not fit in shared memory use that kernel.
+// The result is bit-identical to the single-CTA kernel (same order keys, same tie rule).
+//
+// Rows longer than a 16-CTA cluster holds (16 x 49152 keys, e.g. 1M-token prompts) take two
+// levels: the row is cut into S segments of ~32K keys whose top-k are selected independently (the
+// same kernel on "virtual rows", positions kept absolute), the S*k candidates are gathered in
+// position order, and a second top-k over them picks the final k. Every key of the row's top-k is
+// in its segment's top-k (ties at a segment's cut also go to the lowest positions), and candidate
+// order is position order, so the result equals the one-level selection exactly.
 #include <algorithm>
 #include <cooperative_groups.h>
 
@@ -82,8 +88,16 @@ struct TcSmem {
   int64_t sel_rem, sel_cnt;
 };
 
+// Rows of the selection: value row r (stride n) is cut into `segs` virtual rows of `len` keys (the
+// last one shorter); virtual row vr selects from keys [s * len, s * len + len) of value row
+// vr / segs (s = vr % segs) and writes absolute positions to output row vr. segs = 1, len = n is a
+// plain row-wise selection.
+struct TkRows {
+  int64_t n, len, segs;
+};
+
 template <typename OutT>
-__global__ void __launch_bounds__(TC_THREADS) topk_cluster_kernel(const float* __restrict__ vals, int64_t n,
+__global__ void __launch_bounds__(TC_THREADS) topk_cluster_kernel(const float* __restrict__ vals, TkRows rw,
                                                                   int64_t k, OutT* __restrict__ out,
                                                                   int64_t so_h, int64_t seg) {
   cg::cluster_group cluster = cg::this_cluster();
@@ -92,9 +106,11 @@ __global__ void __launch_bounds__(TC_THREADS) topk_cluster_kernel(const float* _
   const int64_t row = blockIdx.x / C;
   __shared__ TcSmem sm;
   extern __shared__ uint32_t keys[];  // pad(seg) words
-  const float* v = vals + row * n;
+  const int64_t vbase = (row % rw.segs) * rw.len;
+  const int64_t vlen = std::min<int64_t>(rw.len, rw.n - vbase);
+  const float* v = vals + (row / rw.segs) * rw.n + vbase;
   const int64_t lo = (int64_t)cr * seg;
-  const int cnt = (int)std::max<int64_t>(0, std::min<int64_t>(seg, n - lo));
+  const int cnt = (int)std::max<int64_t>(0, std::min<int64_t>(seg, vlen - lo));
   for (int i = threadIdx.x; i < cnt; i += TC_THREADS) keys[pad(i)] = okey(__ldg(v + lo + i));
   // Thread t owns keys [t * E, t * E + E) of the segment.
   const int E = (cnt + TC_THREADS - 1) / TC_THREADS;
@@ -222,7 +238,7 @@ __global__ void __launch_bounds__(TC_THREADS) topk_cluster_kernel(const float* _
     bool take = u > prefix;
     if (u == prefix) take = eq_seen++ < eq_take_t;
     if (take) {
-      if (pos < k) o[pos] = (OutT)(lo + i);
+      if (pos < k) o[pos] = (OutT)(vbase + lo + i);
       ++pos;
     }
   }
@@ -231,15 +247,29 @@ __global__ void __launch_bounds__(TC_THREADS) topk_cluster_kernel(const float* _
 
 }  // namespace
 
-// One cluster of C CTAs per row; a launch the device refuses falls back to the single-CTA kernel.
+namespace {
+
+// Cluster size for `rows` rows of `n` keys: enough CTAs to cover the SMs, segments of at least
+// 4096 keys, at most 16; 0 when a row does not fit one cluster's shared memory.
+int cluster_size(int64_t rows, int64_t n) {
+  int C = 1;
+  while (C < TC_MAX_CLUSTER && rows * C < num_sms() && n / (2 * C) >= 4096) C *= 2;
+  while (C < TC_MAX_CLUSTER && cdiv(n, C) > TC_SEG_MAX) C *= 2;
+  return cdiv(n, C) > TC_SEG_MAX ? 0 : C;
+}
+
+// One cluster of C CTAs per (virtual) row. A launch the device refuses for its configuration
+// (cluster shape or shared memory) falls back to the single-CTA kernel when the rows are plain
+// rows; any other error is reported.
 template <typename OutT>
-int launch_cluster(const float* vals, int64_t rows, int64_t n, int64_t k, OutT* out, int64_t so_h, int C,
-                   int64_t seg, cudaStream_t stream) {
+int launch_cluster(const float* vals, int64_t vrows, TkRows rw, int64_t k, OutT* out, int64_t so_h, int C,
+                   cudaStream_t stream) {
+  const int64_t seg = cdiv(rw.len, C);
   const size_t smem = (size_t)(seg + seg / 32 + 1) * 4;
   cudaFuncSetAttribute(topk_cluster_kernel<OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (C > 8) cudaFuncSetAttribute(topk_cluster_kernel<OutT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(rows * C));
+  cfg.gridDim = dim3((unsigned)(vrows * C));
   cfg.blockDim = dim3(TC_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -250,29 +280,91 @@ int launch_cluster(const float* vals, int64_t rows, int64_t n, int64_t k, OutT* 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, topk_cluster_kernel<OutT>, vals, n, k, out, so_h, seg);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, topk_cluster_kernel<OutT>, vals, rw, k, out, so_h, seg);
   if (e != cudaSuccess) {
-    (void)cudaGetLastError();
-    return topk_single(vals, rows, n, k, out, sizeof(OutT) == 8, so_h, stream);
+    const bool config_error = e == cudaErrorInvalidValue || e == cudaErrorInvalidConfiguration ||
+                              e == cudaErrorInvalidClusterSize || e == cudaErrorLaunchOutOfResources;
+    if (!config_error || rw.segs != 1) return fail(BB_ERR_LAUNCH, "topk_cluster_kernel: %s", cudaGetErrorString(e));
+    (void)cudaGetLastError();  // the refused launch's own error
+    return topk_single(vals, vrows, rw.n, k, out, sizeof(OutT) == 8, so_h, stream);
   }
   count_launch();
   return BB_OK;
 }
 
+// Second level of a long-row selection: candidate values in position order.
+__global__ void topk_gather_kernel(const float* __restrict__ vals, int64_t n, const int32_t* __restrict__ cpos,
+                                   int64_t per_row, float* __restrict__ cval, int64_t total) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
+    cval[i] = __ldg(vals + (i / per_row) * n + cpos[i]);
+}
+template <typename OutT>
+__global__ void topk_map_kernel(const int32_t* __restrict__ sel, const int32_t* __restrict__ cpos, int64_t per_row,
+                                int64_t k, OutT* __restrict__ out, int64_t so_h, int64_t total) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / k;
+    out[r * so_h + i % k] = (OutT)cpos[r * per_row + sel[i]];
+  }
+}
+
+// Segments of a two-level selection (0: the row fits one cluster).
+int64_t long_row_segments(int64_t rows, int64_t n, int64_t k) {
+  if (cluster_size(rows, n) != 0 || k > 4096 || rows * cdiv(n, 32768) * k > ((int64_t)1 << 31)) return 0;
+  return std::max<int64_t>(2, n / 32768);
+}
+
+}  // namespace
+
+size_t topk_scratch_bytes(int64_t rows, int64_t n, int64_t k) {
+  const int64_t S = long_row_segments(rows, n, k);
+  if (S == 0 || k <= 0) return 0;
+  return align_up((size_t)rows * S * k * 4, 256) * 2 + align_up((size_t)rows * k * 4, 256);
+}
+
 // The k largest of each of `rows` rows of n fp32 values, positions ascending (ties at the cut in
 // position order): the routing top-k, also used by KV eviction and decode routing. `out` holds
-// int32 positions, or int64 when out64.
+// int32 positions, or int64 when out64. Rows too long for one cluster use `scratch`
+// (topk_scratch_bytes).
 int topk_sorted(const float* vals, int64_t rows, int64_t n, int64_t k, void* out, bool out64, int64_t so_h,
-                cudaStream_t stream) {
+                void* scratch, size_t scratch_bytes, cudaStream_t stream) {
   if (k <= 0 || rows <= 0 || n <= 0) return BB_OK;
-  // Cluster size: enough CTAs to cover the SMs, segments of at least 4096 keys, at most 16.
-  int C = 1;
-  while (C < TC_MAX_CLUSTER && rows * C < num_sms() && n / (2 * C) >= 4096) C *= 2;
-  while (C < TC_MAX_CLUSTER && cdiv(n, C) > TC_SEG_MAX) C *= 2;
-  const int64_t seg = cdiv(n, C);
-  if (C == 1 || seg > TC_SEG_MAX || rows * C > 65535) return topk_single(vals, rows, n, k, out, out64, so_h, stream);
-  return out64 ? launch_cluster(vals, rows, n, k, static_cast<int64_t*>(out), so_h, C, seg, stream)
-               : launch_cluster(vals, rows, n, k, static_cast<int32_t*>(out), so_h, C, seg, stream);
+  const int64_t S = long_row_segments(rows, n, k);
+  if (S > 0) {
+    if (!scratch || scratch_bytes < topk_scratch_bytes(rows, n, k))
+      return fail(BB_ERR_WORKSPACE, "topk: scratch too small for rows of %lld keys", (long long)n);
+    const int64_t per_row = S * k;
+    char* w = static_cast<char*>(scratch);
+    int32_t* cpos = reinterpret_cast<int32_t*>(w);
+    float* cval = reinterpret_cast<float*>(w + align_up((size_t)rows * per_row * 4, 256));
+    int32_t* sel = reinterpret_cast<int32_t*>(w + 2 * align_up((size_t)rows * per_row * 4, 256));
+    const TkRows seg_rows{n, cdiv(n, S), S};
+    const int C1 = cluster_size(rows * S, seg_rows.len);
+    if (C1 == 0) return fail(BB_ERR_UNSUPPORTED, "topk: segment of %lld keys too long", (long long)seg_rows.len);
+    int st = launch_cluster(vals, rows * S, seg_rows, k, cpos, k, C1, stream);
+    if (st) return st;
+    const int64_t total = rows * per_row;
+    const int blocks = (int)std::min<int64_t>(cdiv(total, 256), 4 * num_sms());
+    topk_gather_kernel<<<blocks, 256, 0, stream>>>(vals, n, cpos, per_row, cval, total);
+    BB_CHECK_LAUNCH("topk_gather_kernel");
+    const int C2 = cluster_size(rows, per_row);
+    if (C2 == 0) return fail(BB_ERR_UNSUPPORTED, "topk: %lld candidates per row", (long long)per_row);
+    st = C2 == 1 ? topk_single(cval, rows, per_row, k, sel, false, k, stream)
+                 : launch_cluster(cval, rows, TkRows{per_row, per_row, 1}, k, sel, k, C2, stream);
+    if (st) return st;
+    const int64_t tk = rows * k;
+    const int b2 = (int)std::min<int64_t>(cdiv(tk, 256), 4 * num_sms());
+    if (out64)
+      topk_map_kernel<<<b2, 256, 0, stream>>>(sel, cpos, per_row, k, static_cast<int64_t*>(out), so_h, tk);
+    else
+      topk_map_kernel<<<b2, 256, 0, stream>>>(sel, cpos, per_row, k, static_cast<int32_t*>(out), so_h, tk);
+    BB_CHECK_LAUNCH("topk_map_kernel");
+    return BB_OK;
+  }
+  const int C = cluster_size(rows, n);
+  if (C <= 1 || rows * C > 65535) return topk_single(vals, rows, n, k, out, out64, so_h, stream);
+  const TkRows rw{n, n, 1};
+  return out64 ? launch_cluster(vals, rows, rw, k, static_cast<int64_t*>(out), so_h, C, stream)
+               : launch_cluster(vals, rows, rw, k, static_cast<int32_t*>(out), so_h, C, stream);
 }
 
 }  // namespace bb
