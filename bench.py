@@ -42,8 +42,8 @@ KERNEL_SOURCES = [ROOT / "utmist_bigger_bird_b200" / "csrc" / f for f in ("flash
 # DRAM traffic of the main-pass kernel, from one ncu capture (dram__bytes_read.sum +
 # dram__bytes_write.sum) of config 2's main pass, and the hash of the kernel sources it was taken
 # on. When the sources change the figure no longer describes the kernel and the bench reports null.
-MAIN_TRAFFIC = {"sources_sha256": "9df179c55d4e9264", "bytes_per_launch": 636.41e6 * (131072 - 256) / (32768 - 256),
-                "capture": "dram__bytes_read.sum + dram__bytes_write.sum of a 32K window-16384 launch (636.4 MB), "
+MAIN_TRAFFIC = {"sources_sha256": "878f07fb37039ee4", "bytes_per_launch": 632.91e6 * (131072 - 256) / (32768 - 256),
+                "capture": "dram__bytes_read.sum + dram__bytes_write.sum of a 32K window-16384 launch (632.9 MB), "
                            "scaled by main-pass query rows x4.024"}
 
 

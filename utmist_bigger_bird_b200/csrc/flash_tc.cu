@@ -105,7 +105,9 @@ __device__ __forceinline__ Sched make_sched(const FlashParams& p, int64_t row0, 
   s.n_rpg = (int)cdiv(p.route_k, BN);
   s.g_lo = s.q_first / p.route_chunk;
   const int64_t g_hi = min(s.q_last / p.route_chunk, p.route_groups - 1);
-  s.n_groups = (p.route_k > 0 && g_hi >= s.g_lo) ? (int)(g_hi - s.g_lo + 1) : 0;
+  // A routed key ps is attended by row q only if front <= ps <= q - W: query tiles whose last row
+  // is within W of the sink's end have no routed steps at all.
+  s.n_groups = (p.route_k > 0 && g_hi >= s.g_lo && s.q_last - p.window >= p.front) ? (int)(g_hi - s.g_lo + 1) : 0;
   s.total = s.n_contig + s.n_groups * s.n_rpg;
   return s;
 }
