@@ -61,6 +61,39 @@ def test_rope_bit_identical(case):
     assert np.array_equal(np32(k), orc.rope(np32(case["k"]), c, s, tag))
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+def test_rope_heads_d128_projection_views(dtype):
+    """head_dim 128 with many heads: q and k as head views of `[1, n, H*d]` projection outputs (the
+    model path's layout), rotated by `rope_inplace` and by `bb_sparse_prefill`'s single q+k launch;
+    both bit-identical to the oracle."""
+    from utmist_bigger_bird_b200 import _ops, rope_inplace
+    from utmist_bigger_bird_b200.attention import route_query_positions
+    from utmist_bigger_bird_b200.workload import rope_tables
+    tag = {torch.bfloat16: "bf16", torch.float16: "f16"}[dtype]
+    n, hq, hk, d = 1000, 32, 8, 128
+    cos, sin = rope_tables(n, d, 500000.0, dtype)
+    g = torch.Generator().manual_seed(12)
+    q0 = torch.randn(1, n, hq * d, generator=g).to(dtype)
+    k0 = torch.randn(1, n, hk * d, generator=g).to(dtype)
+    v0 = torch.randn(1, n, hk * d, generator=g).to(dtype)
+    c, s = np32(cos), np32(sin)
+    want_q = orc.rope(np32(q0.view(1, n, hq, d).transpose(1, 2)), c, s, tag)
+    want_k = orc.rope(np32(k0.view(1, n, hk, d).transpose(1, 2)), c, s, tag)
+    heads = lambda t, h: t.to(DEV).view(1, n, h, d).transpose(1, 2)  # noqa: E731
+    q, k = heads(q0, hq), heads(k0, hk)
+    rope_inplace(q, cos[None].to(DEV), sin[None].to(DEV))
+    rope_inplace(k, cos[None].to(DEV), sin[None].to(DEV))
+    assert np.array_equal(np32(q), want_q) and np.array_equal(np32(k), want_k)
+    q, k, v = heads(q0, hq), heads(k0, hk), heads(v0, hk)
+    out = torch.empty((n, hq, d), device=DEV, dtype=dtype).permute(1, 0, 2)
+    idx = torch.empty((hq, 64), device=DEV, dtype=torch.int32)
+    qpos = route_query_positions(n, 64, "last", 16, 256, DEV)
+    with torch.inference_mode():
+        _ops.sparse_prefill_(q[0], k[0], v[0], qpos, out, idx, sink=16, window=256, budget=64, exact_tail=64,
+                             scaling=d ** -0.5, cos=cos.to(DEV), sin=sin.to(DEV))
+    assert np.array_equal(np32(q), want_q) and np.array_equal(np32(k), want_k)
+
+
 # ----------------------------------------------------------------------------- kernel cases
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])

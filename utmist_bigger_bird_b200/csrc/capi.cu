@@ -47,6 +47,9 @@ int num_sms() {
 int rope_inplace(void* x, int dtype, int64_t B, int64_t H, int64_t T_, int64_t D, int64_t sxb,
                  int64_t sxh, int64_t sxt, const void* cos, const void* sin, int64_t scb,
                  int64_t sct, cudaStream_t stream);
+int rope_pair_inplace(void* q, int64_t hq, int64_t sqh, int64_t sqt, void* k, int64_t hk, int64_t skh, int64_t skt,
+                      int dtype, int64_t T_, int64_t D, const void* cos, const void* sin, int64_t sct,
+                      cudaStream_t stream);
 int routes_workspace_size(const bb_routes_args* a, size_t* bytes);
 int routes(const bb_routes_args* a, void* ws, size_t ws_bytes, cudaStream_t stream);
 int kv_evict_workspace_size(const bb_evict_args* a, size_t* bytes);
@@ -272,9 +275,13 @@ int bb_sparse_prefill(const bb_prefill_args* a, void* ws, size_t ws_bytes, bb_st
   char* w = static_cast<char*>(ws);
   if (a->cos || a->sin) {
     if (!a->cos || !a->sin) return bb::fail(BB_ERR_ARG, "sparse_prefill: cos and sin go together");
-    st = bb::rope_inplace(a->q, a->dtype, 1, a->heads, a->n, a->d, 0, a->sq_h, a->sq_t, a->cos, a->sin, 0, a->sc_t, s);
-    if (st) return st;
-    st = bb::rope_inplace(a->k, a->dtype, 1, a->kv_heads, a->n, a->d, 0, a->sk_h, a->sk_t, a->cos, a->sin, 0, a->sc_t, s);
+    st = bb::rope_pair_inplace(a->q, a->heads, a->sq_h, a->sq_t, a->k, a->kv_heads, a->sk_h, a->sk_t, a->dtype, a->n,
+                               a->d, a->cos, a->sin, a->sc_t, s);
+    if (st == BB_ERR_UNSUPPORTED) {
+      st = bb::rope_inplace(a->q, a->dtype, 1, a->heads, a->n, a->d, 0, a->sq_h, a->sq_t, a->cos, a->sin, 0, a->sc_t, s);
+      if (st) return st;
+      st = bb::rope_inplace(a->k, a->dtype, 1, a->kv_heads, a->n, a->d, 0, a->sk_h, a->sk_t, a->cos, a->sin, 0, a->sc_t, s);
+    }
     if (st) return st;
   }
   st = bb::routes(&pl.ra, w, pl.routes_ws, s);

@@ -102,6 +102,64 @@ __global__ void __launch_bounds__(256) rope_vec16_kernel(T* __restrict__ x, cons
   }
 }
 
+// Up to two tensors (e.g. a layer's q and k) of D = 128 with one cos/sin table: a thread owns one
+// 16-byte chunk pair (i, i + 64) of one position, loads that position's cos/sin vectors once and
+// rotates the chunk of every head of both tensors (heads unrolled by 4 so their loads overlap).
+// Same arithmetic as rope_vec16_kernel; the cos/sin traffic drops from once per head to once per
+// position.
+struct RopeTensor {
+  void* x;
+  int64_t heads, sxh, sxt;
+};
+template <typename T>
+__device__ __forceinline__ void rope_chunk(T* row1, T* row2, const uint4& vc1, const uint4& vc2, const uint4& vs1,
+                                           const uint4& vs2) {
+  using E = Elem<T>;
+  uint4 vx1 = *reinterpret_cast<const uint4*>(row1);
+  uint4 vx2 = *reinterpret_cast<const uint4*>(row2);
+  T* x1 = reinterpret_cast<T*>(&vx1);
+  T* x2 = reinterpret_cast<T*>(&vx2);
+  const T* c1 = reinterpret_cast<const T*>(&vc1);
+  const T* c2 = reinterpret_cast<const T*>(&vc2);
+  const T* s1 = reinterpret_cast<const T*>(&vs1);
+  const T* s2 = reinterpret_cast<const T*>(&vs2);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float a = E::to_f(x1[j]), bq = E::to_f(x2[j]);
+    const float lo = E::round(__fadd_rn(E::round(__fmul_rn(a, E::to_f(c1[j]))),
+                                        E::round(__fmul_rn(-bq, E::to_f(s1[j])))));
+    const float hi = E::round(__fadd_rn(E::round(__fmul_rn(bq, E::to_f(c2[j]))),
+                                        E::round(__fmul_rn(a, E::to_f(s2[j])))));
+    x1[j] = E::from_f(lo);
+    x2[j] = E::from_f(hi);
+  }
+  *reinterpret_cast<uint4*>(row1) = vx1;
+  *reinterpret_cast<uint4*>(row2) = vx2;
+}
+template <typename T>
+__global__ void __launch_bounds__(256) rope_heads_kernel(RopeTensor t0, RopeTensor t1, const T* __restrict__ cos,
+                                                         const T* __restrict__ sin, int64_t T_, int64_t sct) {
+  const int64_t total = T_ * 8;
+  for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < total;
+       w += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = w % 8, t = w / 8;
+    const T* cr = cos + t * sct + c * 8;
+    const T* sr = sin + t * sct + c * 8;
+    const uint4 vc1 = __ldg(reinterpret_cast<const uint4*>(cr));
+    const uint4 vc2 = __ldg(reinterpret_cast<const uint4*>(cr + 64));
+    const uint4 vs1 = __ldg(reinterpret_cast<const uint4*>(sr));
+    const uint4 vs2 = __ldg(reinterpret_cast<const uint4*>(sr + 64));
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const RopeTensor& rt = u ? t1 : t0;
+      if (!rt.x) continue;
+      T* base = static_cast<T*>(rt.x) + t * rt.sxt + c * 8;
+#pragma unroll 4
+      for (int64_t h = 0; h < rt.heads; ++h) rope_chunk<T>(base + h * rt.sxh, base + h * rt.sxh + 64, vc1, vc2, vs1, vs2);
+    }
+  }
+}
+
 template <typename T>
 int launch_rope(void* x, int64_t B, int64_t H, int64_t T_, int64_t D, int64_t sxb, int64_t sxh,
                 int64_t sxt, const void* cos, const void* sin, int64_t scb, int64_t sct,
@@ -109,6 +167,15 @@ int launch_rope(void* x, int64_t B, int64_t H, int64_t T_, int64_t D, int64_t sx
   const int64_t half = D / 2;
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if constexpr (sizeof(T) == 2) {
+    if (B == 1 && D == 128 && H > 1 && al16(x) && al16(cos) && al16(sin) && (sxh * 2) % 16 == 0 &&
+        (sxt * 2) % 16 == 0 && (sct * 2) % 16 == 0) {
+      if (T_ == 0) return BB_OK;
+      const int64_t grid = std::min<int64_t>(cdiv(T_ * 8, 256), (int64_t)num_sms() * 16);
+      rope_heads_kernel<T><<<grid, 256, 0, stream>>>(RopeTensor{x, H, sxh, sxt}, RopeTensor{nullptr, 0, 0, 0},
+                                                     static_cast<const T*>(cos), static_cast<const T*>(sin), T_, sct);
+      BB_CHECK_LAUNCH("rope_heads_kernel");
+      return BB_OK;
+    }
     if (half % 8 == 0 && al16(x) && al16(cos) && al16(sin) && (sxb * 2) % 16 == 0 && (sxh * 2) % 16 == 0 &&
         (sxt * 2) % 16 == 0 && (scb * 2) % 16 == 0 && (sct * 2) % 16 == 0) {
       const int64_t total = B * H * T_ * (half / 8);
@@ -139,6 +206,28 @@ int launch_rope(void* x, int64_t B, int64_t H, int64_t T_, int64_t D, int64_t sx
 }
 
 }  // namespace
+
+// q and k of one layer (batch 1, D = 128, 16-bit, rows on 16-byte boundaries) with one table in one
+// launch; returns BB_ERR_UNSUPPORTED when the layout does not qualify (callers then rotate each).
+int rope_pair_inplace(void* q, int64_t hq, int64_t sqh, int64_t sqt, void* k, int64_t hk, int64_t skh, int64_t skt,
+                      int dtype, int64_t T_, int64_t D, const void* cos, const void* sin, int64_t sct,
+                      cudaStream_t stream) {
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (D != 128 || (dtype != BB_BF16 && dtype != BB_F16) || !al16(q) || !al16(k) || !al16(cos) || !al16(sin) ||
+      (sqh * 2) % 16 || (sqt * 2) % 16 || (skh * 2) % 16 || (skt * 2) % 16 || (sct * 2) % 16)
+    return BB_ERR_UNSUPPORTED;
+  if (T_ == 0) return BB_OK;
+  const int64_t grid = std::min<int64_t>(cdiv(T_ * 8, 256), (int64_t)num_sms() * 16);
+  const RopeTensor a{q, hq, sqh, sqt}, b{k, hk, skh, skt};
+  if (dtype == BB_BF16)
+    rope_heads_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(a, b, static_cast<const __nv_bfloat16*>(cos),
+                                                               static_cast<const __nv_bfloat16*>(sin), T_, sct);
+  else
+    rope_heads_kernel<__half><<<grid, 256, 0, stream>>>(a, b, static_cast<const __half*>(cos),
+                                                        static_cast<const __half*>(sin), T_, sct);
+  BB_CHECK_LAUNCH("rope_heads_kernel");
+  return BB_OK;
+}
 
 int rope_inplace(void* x, int dtype, int64_t B, int64_t H, int64_t T_, int64_t D, int64_t sxb,
                  int64_t sxh, int64_t sxt, const void* cos, const void* sin, int64_t scb,
