@@ -42,9 +42,10 @@ KERNEL_SOURCES = [ROOT / "utmist_bigger_bird_b200" / "csrc" / f for f in ("flash
 # DRAM traffic of the main-pass kernel, from one ncu capture (dram__bytes_read.sum +
 # dram__bytes_write.sum) of config 2's main pass, and the hash of the kernel sources it was taken
 # on. When the sources change the figure no longer describes the kernel and the bench reports null.
-MAIN_TRAFFIC = {"sources_sha256": "878f07fb37039ee4", "bytes_per_launch": 632.91e6 * (131072 - 256) / (32768 - 256),
-                "capture": "dram__bytes_read.sum + dram__bytes_write.sum of a 32K window-16384 launch (632.9 MB), "
-                           "scaled by main-pass query rows x4.024"}
+MAIN_TRAFFIC = {"sources_sha256": "878f07fb37039ee4", "bytes_per_launch": 635.29e6 * (131072 - 256) / (32768 - 256),
+                "capture": "dram__bytes_read.sum + dram__bytes_write.sum of the main pass of "
+                           "`bench.py --config sweep_n32768_w16384 --part layer` (635.3 MB), scaled by main-pass "
+                           "query rows x4.024"}
 
 
 def sources_sha256():
@@ -546,6 +547,20 @@ def run_ours(args):
     traffic, traffic_src = main_traffic(cfg, per)
     route_bytes = per * n * d * 2 + H * min(cfg.n_route, n) * d * 2 + H * budget * 4
     route_gbs = route_bytes / (route_ms * 1e-3) / 1e9
+    if args.part == "layer":
+        # The layer and its kernels only (no side paths, comparators, e2e or CPU sample): the
+        # committed command the ncu captures of these kernels run.
+        main_max, _ = reduce_step(main_ms, 0.0, dev)
+        if world > 1:
+            dist.barrier(device_ids=[local])
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"part": "layer", "workload": cfg.name, "n_gpus": world, "ms_per_step": ms_max,
+                              "eff_tflops": value, "main_ms": main_max, "main_tflops": achieved,
+                              "main_frac": achieved / pk["bf16_tflops"], "routing_ms": route_ms,
+                              "exact_tail_ms": tail_ms, "gpu_launches": int(launches), "clocks": clock}),
+                  flush=True)
+        return
 
     evict_line, decode_line = side_paths(cfg, qr, kr, v, idx, qpos, budget, dev, stream, reps, pk)
 
@@ -806,9 +821,10 @@ def main():
                    help="time rank R's share of an N-way KV-head split alone on this one GPU (no process "
                         "group): the per-rank step of --gpus N, for a config whose whole layer needs more "
                         "GPUs (or memory) than one")
-    p.add_argument("--part", default="all", choices=["all", "decode", "evict", "model"],
-                   help="time one side path alone (1 GPU) instead of the full benchmark; 'model' = the "
-                        "whole-model prefill with and without the sparse path and memory savers")
+    p.add_argument("--part", default="all", choices=["all", "layer", "decode", "evict", "model"],
+                   help="time one side path alone (1 GPU) instead of the full benchmark; 'layer' = the layer "
+                        "steps and its kernels timed alone, nothing else; 'model' = the whole-model prefill "
+                        "with and without the sparse path and memory savers")
     p.add_argument("--model-tokens", type=int, default=131072, help="--part model: prompt length")
     p.add_argument("--model-layers", type=int, default=32, help="--part model: decoder layers")
     p.add_argument("--model-norm", default="fused", choices=["fused", "chunked"],
@@ -819,7 +835,7 @@ def main():
     args = p.parse_args()
     if args.part == "model":
         run_model(args)
-    elif args.part != "all":
+    elif args.part not in ("all", "layer"):
         run_part(args)
     elif args.impl == "reference":
         run_reference(args)
