@@ -139,6 +139,9 @@ BB_API int bb_routes_noalloc(const bb_routes_args* a, bb_stream_t stream);
  * + (h % num_heads) / kv_groups. token_mask (optional, [B, n] bytes, B = BH / num_heads) drops
  * masked keys and zeroes masked query rows. Fully masked rows give 0.
  * Rows [row_begin, row_end) of T are computed and written; other output rows are untouched.
+ * Workspace (bb_flash_workspace_size): split partials of long-key-range calls and, for head_dim
+ * 128 with routes, the call's routed K/V rows gathered once ([BH, G, K rounded up to 128, D]
+ * each), so that the kernel loads routed tiles like window tiles.
  */
 typedef struct {
   const void* q;  int64_t sq_h, sq_t;       /* [BH, T, D] */

@@ -26,9 +26,16 @@ struct FlashParams {
   float2* part_ml;             // [splits][BH][T]: (running max in log2 units, sum)
   int64_t bh;
   uint32_t serial;             // launch serial (cross-CTA abort of the tcgen05 kernels)
+  // tcgen05 path: routed K/V rows gathered once per call, [bh][route_groups][route_kpad][128] each
+  // (route_kpad = route_k rounded up to 128; empty slots are zero rows).
+  void* kg;
+  void* vg;
+  int64_t route_kpad;
 };
 
 int flash_tc_launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream);
+// Bytes of the tcgen05 path's gathered routed rows (K and V together; 0 without routes).
+size_t flash_tc_gather_bytes(const bb_flash_args* a);
 int flash_tc_splits(const bb_flash_args* a, int sms);
 // Read and clear the current device's fault words (set by a kernel whose bounded wait gave up):
 // one for the attention kernels, one for the tcgen05 routing kernels.

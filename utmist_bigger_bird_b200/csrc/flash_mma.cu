@@ -408,6 +408,7 @@ int flash_workspace_size(const bb_flash_args* a, size_t* bytes) {
   *bytes = splits > 1 ? align_up((size_t)splits * a->bh * a->t * dpad_of(a->d) * 4, 256) +
                             align_up((size_t)splits * a->bh * a->t * 8, 256)
                       : 0;
+  if (use_tc(a)) *bytes += flash_tc_gather_bytes(a);
   return BB_OK;
 }
 
@@ -439,7 +440,13 @@ int flash(const bb_flash_args* a, void* ws, size_t ws_bytes, cudaStream_t stream
   const int dp = dpad_of(a->d);
   char* w = static_cast<char*>(ws);
   p.part_acc = reinterpret_cast<float*>(w);
+  const size_t split_bytes = p.splits > 1 ? align_up((size_t)p.splits * a->bh * a->t * dp * 4, 256) +
+                                                align_up((size_t)p.splits * a->bh * a->t * 8, 256)
+                                          : 0;
   p.part_ml = reinterpret_cast<float2*>(w + (p.splits > 1 ? align_up((size_t)p.splits * a->bh * a->t * dp * 4, 256) : 0));
+  p.route_kpad = cdiv(a->route_k, 128) * 128;
+  p.kg = use_tc(a) && a->route_k > 0 ? w + split_bytes : nullptr;
+  p.vg = p.kg ? w + split_bytes + flash_tc_gather_bytes(a) / 2 : nullptr;
   if (use_tc(a)) return flash_tc_launch(a, p, stream);
   if (a->dtype == BB_BF16) {
     if (dp == 32) return launch_flash_t<__nv_bfloat16, 32>(a, p, stream);

@@ -10,8 +10,8 @@
 // key range for the exact tail); used for odd GQA groups. flash_tc_pair_kernel (further below)
 // computes two query heads of one KV head per CTA and is used otherwise. flash_tc_kernel, 192
 // threads:
-//   warp 0      producer: Q, and every contiguous (sink/window) K/V tile by TMA (128B swizzle);
-//               routed K/V rows gathered with cp.async into the same swizzled layout.
+//   warp 0      producer: Q and every K/V tile by TMA (128B swizzle): sink/window tiles from K/V,
+//               routed tiles from the call's gathered routed rows (route_gather_kernel).
 //   warp 1      allocates TMEM and issues the MMAs (one elected lane):
 //                 S_j = Q K_j^T   (SS: A = Q smem K-major, B = K smem K-major) into S[j % 2]
 //                 O  += P_j V_j   (TS: A = P in TMEM over S[j % 2], B = V smem MN-major) into O
@@ -198,8 +198,40 @@ __device__ __forceinline__ void mask_cols128(float* s, int kind, const MaskLimit
 
 struct TcMaps {
   CUtensorMap q, k, v;
+  CUtensorMap kg, vg;   // gathered routed rows [bh * route_groups * route_kpad][128] (when routed)
   int q_swap, kv_swap;  // 1: the map's dims are {d, heads, rows} (coordinates swapped)
 };
+
+// Routed K/V rows of every (head, route group, slot), gathered once per call into two contiguous
+// [bh][route_groups][route_kpad][128] arrays, so that the attention kernels load a routed tile
+// with two tiled TMA boxes like a window tile instead of gathering the same rows again for every
+// query tile. One thread per 16-byte chunk; empty slots and the padding to 128 are zero rows
+// (the kernels mask them by position anyway).
+template <typename T>
+__global__ void __launch_bounds__(256) route_gather_kernel(FlashParams p) {
+  const int64_t rows = p.bh * p.route_groups * p.route_kpad;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < rows * 16;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i >> 4, c = i & 15;
+    const int64_t slot = r % p.route_kpad, g = (r / p.route_kpad) % p.route_groups;
+    const int64_t h = r / (p.route_kpad * p.route_groups);
+    const int64_t kvh = (h / p.num_heads) * (p.num_heads / p.kv_groups) + (h % p.num_heads) / p.kv_groups;
+    const int64_t ps = routed_pos(p, h, g, slot);
+    uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
+    if (ps >= 0) {
+      kv = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.k) + kvh * p.sk_h + ps * p.sk_t) + c);
+      vv = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.v) + kvh * p.sv_h + ps * p.sv_t) + c);
+    }
+    reinterpret_cast<uint4*>(p.kg)[i] = kv;
+    reinterpret_cast<uint4*>(p.vg)[i] = vv;
+  }
+}
+
+// Row of the gathered arrays where head h's 128-slot routed tile starting at slot0 of group g
+// begins.
+__device__ __forceinline__ int gathered_row(const FlashParams& p, int64_t h, int64_t g, int64_t slot0) {
+  return (int)((h * p.route_groups + g) * p.route_kpad + slot0);
+}
 
 template <typename T>
 __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_constant__ TcMaps maps, FlashParams p) {
@@ -267,8 +299,6 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
         }
       }
       q_issued = true;
-      const T* kbase = static_cast<const T*>(p.k) + kvh * p.sk_h;
-      const T* vbase = static_cast<const T*>(p.v) + kvh * p.sv_h;
       for (int it = 0; it < 2 * nt; ++it) {
         const int j = it >> 1;
         const bool is_v = it & 1;
@@ -291,23 +321,11 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
             }
           }
         } else {
-          // Gather 128 routed rows (16 chunks of 16 bytes each) into the 128B-swizzled layout.
-          const T* src_base = is_v ? vbase : kbase;
-          const int64_t sstride = is_v ? p.sv_t : p.sk_t;
-          for (int r = lane; r < BN; r += 32) {
-            const int64_t ps = routed_pos(p, h, tl.group, tl.slot0 + r);
-            const T* row = src_base + (ps < 0 ? 0 : ps) * sstride;
-#pragma unroll
-            for (int c = 0; c < 16; ++c) {
-              const uint32_t d = dst + (uint32_t)(c >> 3) * HALF + (uint32_t)r * 128u +
-                                 (uint32_t)(((c & 7) ^ (r & 7)) << 4);
-              cp_async_16(d, row + c * 8, ps >= 0);
-            }
-          }
-          asm volatile("cp.async.wait_all;" ::: "memory");
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          __syncwarp();
-          mbar_arrive_one(bar(B_FULL + b));
+          const CUtensorMap* m = is_v ? &maps.vg : &maps.kg;
+          const int row = gathered_row(p, h, tl.group, tl.slot0);
+          mbar_expect_tx_one(bar(B_FULL + b), TILE);
+          tma_load_3d_one(dst, m, 0, row, 0, bar(B_FULL + b));
+          tma_load_3d_one(dst + HALF, m, 64, row, 0, bar(B_FULL + b));
         }
         ++fills[b];
       }
@@ -606,85 +624,36 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
             }
           }
         }
-        const T* kbase = static_cast<const T*>(p.k) + kvh * p.sk_h;
-        const T* vbase = static_cast<const T*>(p.v) + kvh * p.sv_h;
         int it = 0;
-        bool ok = true;
-        // Shared steps: K_j then V_j, each a pair of tiled TMA loads.
-        for (int j = 0; ok && j < fl.shared; ++j) {
+        // One loop over the fills: a shared step loads K_j then V_j from the K/V maps, a routed step
+        // K_A, K_B, V_A, V_B from the gathered routed rows (route_gather_kernel); each fill is two
+        // tiled TMA boxes.
+        const int n_fills = 2 * fl.shared + 4 * (nt - fl.shared);
+        for (; it < n_fills; ++it) {
+          const int b = it % PNB;
+          const int round = it / PNB;
+          if (round > 0 && !mbar_wait_warp(bar(PB_EMPTY + b), (round - 1) & 1, abort_flag, F_PROD_EMPTY)) break;
+          const bool routed = it >= 2 * fl.shared;
+          const int f = routed ? (it - 2 * fl.shared) & 3 : it & 1;
+          const int j = routed ? fl.shared + ((it - 2 * fl.shared) >> 2) : it >> 1;
           const Tile tl = tile_at(p, sc, t_begin + j);
-          for (int f = 0; f < 2; ++f, ++it) {
-            const int b = it % PNB;
-            const int round = it / PNB;
-            if (round > 0 && !mbar_wait_warp(bar(PB_EMPTY + b), (round - 1) & 1, abort_flag, F_PROD_EMPTY)) {
-              ok = false;
-              break;
-            }
-            const uint32_t dst = sbase + P_SM_KV + (uint32_t)b * TILE;
-            const CUtensorMap* m = f ? &maps.v : &maps.k;
-            const int c1 = (int)tl.k0, c2 = (int)kvh;
-            mbar_expect_tx_one(bar(PB_FULL + b), TILE);
-            if (maps.kv_swap) {
-              tma_load_3d_one(dst, m, 0, c2, c1, bar(PB_FULL + b));
-              tma_load_3d_one(dst + HALF, m, 64, c2, c1, bar(PB_FULL + b));
-            } else {
-              tma_load_3d_one(dst, m, 0, c1, c2, bar(PB_FULL + b));
-              tma_load_3d_one(dst + HALF, m, 64, c1, c2, bar(PB_FULL + b));
-            }
-            ++fills[b];
+          const CUtensorMap* m = routed ? (f >= 2 ? &maps.vg : &maps.kg) : (f ? &maps.v : &maps.k);
+          int c1, c2;
+          if (routed) {
+            c1 = gathered_row(p, hA + (f & 1), tl.group, tl.slot0);
+            c2 = 0;
+          } else if (maps.kv_swap) {
+            c1 = (int)kvh;
+            c2 = (int)tl.k0;
+          } else {
+            c1 = (int)tl.k0;
+            c2 = (int)kvh;
           }
-        }
-        // Routed steps: K_A, K_B, V_A, V_B, each 128 rows gathered with cp.async (16 chunks of 16
-        // bytes per row) into the 128B-swizzled layout. The copies complete asynchronously on the
-        // slot's full barrier (cp.async.mbarrier.arrive from every lane, then one regular arrive),
-        // so the warp goes on issuing the next gathers instead of waiting for each; the positions of
-        // the next step are loaded while this step's copies are in flight.
-        if (ok && fl.shared < nt) {
-          int32_t pos[2][4], nxt[2][4];
-          auto load_pos = [&](int j, int32_t (&dst)[2][4]) {
-            const Tile tl = tile_at(p, sc, t_begin + j);
-#pragma unroll
-            for (int w = 0; w < 2; ++w)
-#pragma unroll
-              for (int i = 0; i < 4; ++i) dst[w][i] = (int32_t)routed_pos(p, hA + w, tl.group, tl.slot0 + lane + 32 * i);
-          };
-          load_pos(fl.shared, pos);
-          for (int j = fl.shared; ok && j < nt; ++j) {
-            for (int f = 0; f < 4; ++f, ++it) {
-              const int b = it % PNB;
-              const int round = it / PNB;
-              if (round > 0 && !mbar_wait_warp(bar(PB_EMPTY + b), (round - 1) & 1, abort_flag, F_PROD_EMPTY)) {
-                ok = false;
-                break;
-              }
-              const uint32_t dst = sbase + P_SM_KV + (uint32_t)b * TILE;
-              const T* src_base = f >= 2 ? vbase : kbase;
-              const int64_t sstride = f >= 2 ? p.sv_t : p.sk_t;
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int r = lane + 32 * i;
-                const int32_t ps = (f & 1) ? pos[1][i] : pos[0][i];
-                const T* row = src_base + (int64_t)(ps < 0 ? 0 : ps) * sstride;
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                  const uint32_t d = dst + (uint32_t)(c >> 3) * HALF + (uint32_t)r * 128u +
-                                     (uint32_t)(((c & 7) ^ (r & 7)) << 4);
-                  cp_async_16(d, row + c * 8, ps >= 0);
-                }
-              }
-              asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar(PB_FULL + b)) : "memory");
-              __syncwarp();
-              mbar_arrive_one(bar(PB_FULL + b));
-              ++fills[b];
-            }
-            if (ok && j + 1 < nt) {
-              load_pos(j + 1, nxt);
-#pragma unroll
-              for (int w = 0; w < 2; ++w)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) pos[w][i] = nxt[w][i];
-            }
-          }
+          const uint32_t dst = sbase + P_SM_KV + (uint32_t)b * TILE;
+          mbar_expect_tx_one(bar(PB_FULL + b), TILE);
+          tma_load_3d_one(dst, m, 0, c1, c2, bar(PB_FULL + b));
+          tma_load_3d_one(dst + HALF, m, 64, c1, c2, bar(PB_FULL + b));
+          ++fills[b];
         }
       }
       {
@@ -706,11 +675,10 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
       };
       // O_w += P_w(i) V in two K halves (keys 0-63, 64-127), each issued as soon as the softmax has
       // stored that half of P. `fv` is V's fill number; `wait_v`: wait for it (head A always, head B
-      // only for its own gathered V); `gathered`: cp.async-filled, fenced to the async proxy.
-      auto pv = [&](int w, int i, int fv, bool wait_v, bool gathered) -> bool {
+      // only for its own routed V).
+      auto pv = [&](int w, int i, int fv, bool wait_v) -> bool {
         if (!mbar_wait_warp(bar(PB_P + 2 * w), i & 1, abort_flag, F_MMA_P)) return false;
         if (wait_v && !full_wait(fv, F_MMA_V)) return false;
-        if (gathered) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         tc_fence_after();
         const uint32_t vb = sbase + P_SM_KV + slot_of(fv) * TILE;
         const uint32_t od = tmem + 256u + (uint32_t)w * 128u, pa = tmem + (uint32_t)w * 128u;
@@ -737,9 +705,9 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
         tc_fence_after();
         const uint32_t kb = sbase + P_SM_KV + slot_of(fk) * TILE;
         if (j > 0) {
-          if (!(ok = pv(0, j - 1, fk - 1, true, false))) break;
+          if (!(ok = pv(0, j - 1, fk - 1, true))) break;
           s_mma(0, kb);
-          if (!(ok = pv(1, j - 1, fk - 1, false, false))) break;
+          if (!(ok = pv(1, j - 1, fk - 1, false))) break;
           mma_commit_one(bar(PB_EMPTY + slot_of(fk - 1)));  // V_{j-1} consumed by both heads
           s_mma(1, kb);
         } else {
@@ -755,16 +723,15 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
           ok = false;
           break;
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         tc_fence_after();
         if (j > 0) {
           const bool prev_routed = j - 1 >= c;
           const int fva = prev_routed ? F - 2 : F - 1, fvb = F - 1;
-          if (!(ok = pv(0, j - 1, fva, true, prev_routed))) break;
+          if (!(ok = pv(0, j - 1, fva, true))) break;
           if (prev_routed) mma_commit_one(bar(PB_EMPTY + slot_of(fva)));
           s_mma(0, sbase + P_SM_KV + slot_of(F) * TILE);
           mma_commit_one(bar(PB_EMPTY + slot_of(F)));
-          if (!(ok = pv(1, j - 1, fvb, prev_routed, prev_routed))) break;
+          if (!(ok = pv(1, j - 1, fvb, prev_routed))) break;
           mma_commit_one(bar(PB_EMPTY + slot_of(fvb)));
         } else {
           s_mma(0, sbase + P_SM_KV + slot_of(F) * TILE);
@@ -774,7 +741,6 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
           ok = false;
           break;
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         tc_fence_after();
         s_mma(1, sbase + P_SM_KV + slot_of(F + 1) * TILE);
         mma_commit_one(bar(PB_EMPTY + slot_of(F + 1)));
@@ -783,13 +749,13 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
         const int last = nt - 1;
         if (last < c) {
           const int fv = 2 * last + 1;
-          if (pv(0, last, fv, true, false) && pv(1, last, fv, false, false))
+          if (pv(0, last, fv, true) && pv(1, last, fv, false))
             mma_commit_one(bar(PB_EMPTY + slot_of(fv)));
         } else {
           const int F = 2 * c + 4 * (last - c);
-          if (pv(0, last, F + 2, true, true)) {
+          if (pv(0, last, F + 2, true)) {
             mma_commit_one(bar(PB_EMPTY + slot_of(F + 2)));
-            if (pv(1, last, F + 3, true, true)) mma_commit_one(bar(PB_EMPTY + slot_of(F + 3)));
+            if (pv(1, last, F + 3, true)) mma_commit_one(bar(PB_EMPTY + slot_of(F + 3)));
           }
         }
       }
@@ -1040,6 +1006,20 @@ int launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream) {
   if (st) return st;
   if (sk != sv) return fail(BB_ERR_STRIDE, "flash: K and V views must have the same dimension order");
   maps.kv_swap = sk;
+  maps.kg = maps.k;  // unused without routes
+  maps.vg = maps.v;
+  if (p.kg) {
+    const int64_t rows = p.bh * p.route_groups * p.route_kpad;
+    if (rows > 0x7fffffffLL) return fail(BB_ERR_UNSUPPORTED, "flash: too many routed rows (%lld)", (long long)rows);
+    int unused = 0;
+    st = make_map(&maps.kg, &unused, p.kg, a->dtype, 1, rows, 0, 128);
+    if (st) return st;
+    st = make_map(&maps.vg, &unused, p.vg, a->dtype, 1, rows, 0, 128);
+    if (st) return st;
+    const int64_t grid = std::min<int64_t>(cdiv(rows * 16, 256), (int64_t)num_sms() * 8);
+    route_gather_kernel<T><<<(unsigned)grid, 256, 0, stream>>>(p);
+    BB_CHECK_LAUNCH("route_gather_kernel");
+  }
   if (pair_mode(a)) {
     cudaFuncSetAttribute(flash_tc_pair_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SM_ALLOC);
     dim3 grid((unsigned)cdiv(a->row_end - a->row_begin, BM), (unsigned)(a->bh / 2), (unsigned)p.splits);
@@ -1078,6 +1058,11 @@ int flash_tc_splits(const bb_flash_args* a, int sms) {
     }
   }
   return best;
+}
+
+size_t flash_tc_gather_bytes(const bb_flash_args* a) {
+  if (a->route_k <= 0) return 0;
+  return 2 * align_up((size_t)a->bh * a->route_groups * cdiv(a->route_k, tc::BN) * tc::BN * 128 * 2, 256);
 }
 
 int flash_tc_launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream) {
