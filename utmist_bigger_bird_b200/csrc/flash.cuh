@@ -31,6 +31,8 @@ struct FlashParams {
   void* kg;
   void* vg;
   int64_t route_kpad;
+  int32_t* tile_min;           // [bh][route_groups][route_kpad / 128]: smallest routed position >= front
+                               // (read as unsigned; all ones = none)
 };
 
 int flash_tc_launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream);

@@ -445,8 +445,9 @@ int flash(const bb_flash_args* a, void* ws, size_t ws_bytes, cudaStream_t stream
                                           : 0;
   p.part_ml = reinterpret_cast<float2*>(w + (p.splits > 1 ? align_up((size_t)p.splits * a->bh * a->t * dp * 4, 256) : 0));
   p.route_kpad = cdiv(a->route_k, 128) * 128;
-  p.kg = use_tc(a) && a->route_k > 0 ? w + split_bytes : nullptr;
-  p.vg = p.kg ? w + split_bytes + flash_tc_gather_bytes(a) / 2 : nullptr;
+  p.kg = use_tc(a) && a->route_k > 0 ? w + split_bytes : nullptr;  // the tcgen05 launch lays out the rest
+  p.vg = nullptr;
+  p.tile_min = nullptr;
   if (use_tc(a)) return flash_tc_launch(a, p, stream);
   if (a->dtype == BB_BF16) {
     if (dp == 32) return launch_flash_t<__nv_bfloat16, 32>(a, p, stream);

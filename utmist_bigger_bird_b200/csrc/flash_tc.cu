@@ -75,6 +75,10 @@ struct Sched {
   int n_a, w_lo, n_w, n_contig;   // contiguous tile indices: [0, n_a) and [w_lo, w_lo + n_w)
   int64_t g_lo;
   int n_rpg, n_groups, total;
+  // Routed tiles k = (group - g_lo) * n_rpg + r kept in the schedule (bit k), when the call's
+  // per-tile minimum positions are known and there are at most 64 routed tiles; else all are kept.
+  bool skip;
+  uint64_t live;
 };
 
 struct Tile {
@@ -84,7 +88,8 @@ struct Tile {
   bool masked;
 };
 
-__device__ __forceinline__ Sched make_sched(const FlashParams& p, int64_t row0, int64_t row1) {
+// h0, nh: the query heads of the CTA (a routed step holds tile r of each of them).
+__device__ __forceinline__ Sched make_sched(const FlashParams& p, int64_t row0, int64_t row1, int64_t h0, int nh) {
   Sched s;
   s.q_first = p.offset + row0;
   s.q_last = p.offset + row1 - 1;
@@ -109,7 +114,35 @@ __device__ __forceinline__ Sched make_sched(const FlashParams& p, int64_t row0, 
   // is within W of the sink's end have no routed steps at all.
   s.n_groups = (p.route_k > 0 && g_hi >= s.g_lo && s.q_last - p.window >= p.front) ? (int)(g_hi - s.g_lo + 1) : 0;
   s.total = s.n_contig + s.n_groups * s.n_rpg;
+  // A routed tile none of whose keys any row of the query tile can attend (its smallest key at or
+  // after the sink, from route_gather_kernel, lies beyond q_last - W for every head of the CTA) is
+  // left out of the schedule: its step would be masked entirely.
+  s.skip = false;
+  s.live = 0;
+  const int nrt = s.n_groups * s.n_rpg;
+  if (p.tile_min && nrt > 0 && nrt <= 64) {
+    const int64_t lim = s.q_last - p.window;
+    uint64_t m = 0;
+    for (int k = 0; k < nrt; ++k) {
+      const int64_t g = s.g_lo + k / s.n_rpg;
+      const int r = k % s.n_rpg;
+      bool live = false;
+      for (int e = 0; e < nh; ++e)
+        live |= (int64_t)(uint32_t)p.tile_min[((h0 + e) * p.route_groups + g) * s.n_rpg + r] <= lim;
+      if (live) m |= 1ull << k;
+    }
+    s.skip = true;
+    s.live = m;
+    s.total = s.n_contig + __popcll(m);
+  }
   return s;
+}
+
+// Index of the r-th set bit of m (r < popcount(m)).
+__device__ __forceinline__ int nth_bit(uint64_t m, int r) {
+  const uint32_t lo = (uint32_t)m;
+  const int c = __popc(lo);
+  return r < c ? (int)__fns(lo, 0, r + 1) : 32 + (int)__fns((uint32_t)(m >> 32), 0, r - c + 1);
 }
 
 __device__ __forceinline__ Tile tile_at(const FlashParams& p, const Sched& s, int t) {
@@ -125,7 +158,7 @@ __device__ __forceinline__ Tile tile_at(const FlashParams& p, const Sched& s, in
     const bool window_all = tl.k0 >= s.q_last - p.window + 1;
     tl.masked = !(causal_ok && (sink_all || window_all)) || p.mask != nullptr;
   } else {
-    const int r = t - s.n_contig;
+    const int r = s.skip ? nth_bit(s.live, t - s.n_contig) : t - s.n_contig;
     tl.kind = 1;
     tl.k0 = 0;
     tl.group = s.g_lo + r / s.n_rpg;
@@ -206,7 +239,9 @@ struct TcMaps {
 // [bh][route_groups][route_kpad][128] arrays, so that the attention kernels load a routed tile
 // with two tiled TMA boxes like a window tile instead of gathering the same rows again for every
 // query tile. One thread per 16-byte chunk; empty slots and the padding to 128 are zero rows
-// (the kernels mask them by position anyway).
+// (the kernels mask them by position anyway). It also records, per 128-slot routed tile, the
+// smallest position at or after the sink (tile_min, preset to all ones), which lets the
+// attention kernels leave out routed tiles that no row of a query tile can attend.
 template <typename T>
 __global__ void __launch_bounds__(256) route_gather_kernel(FlashParams p) {
   const int64_t rows = p.bh * p.route_groups * p.route_kpad;
@@ -217,6 +252,8 @@ __global__ void __launch_bounds__(256) route_gather_kernel(FlashParams p) {
     const int64_t h = r / (p.route_kpad * p.route_groups);
     const int64_t kvh = (h / p.num_heads) * (p.num_heads / p.kv_groups) + (h % p.num_heads) / p.kv_groups;
     const int64_t ps = routed_pos(p, h, g, slot);
+    if (c == 0 && ps >= p.front)
+      atomicMin(reinterpret_cast<unsigned int*>(p.tile_min) + (r >> 7), (unsigned int)ps);
     uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
     if (ps >= 0) {
       kv = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.k) + kvh * p.sk_h + ps * p.sk_t) + c);
@@ -250,7 +287,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
   const int64_t row1 = min(row0 + BM, p.row_end);
   const int64_t kvh = (h / p.num_heads) * (p.num_heads / p.kv_groups) + (h % p.num_heads) / p.kv_groups;
   const int64_t batch = h / p.num_heads;
-  const Sched sc = make_sched(p, row0, row1);
+  const Sched sc = make_sched(p, row0, row1, h, 1);
   const int t_begin = (int)((int64_t)sc.total * split / p.splits);
   const int nt = (int)((int64_t)sc.total * (split + 1) / p.splits) - t_begin;
 
@@ -571,7 +608,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
   const int64_t row0 = p.row_begin + (int64_t)blockIdx.x * BM;
   const int64_t row1 = min(row0 + BM, p.row_end);
   const int64_t kvh = (hA / p.num_heads) * (p.num_heads / p.kv_groups) + (hA % p.num_heads) / p.kv_groups;
-  const Sched sc = make_sched(p, row0, row1);
+  const Sched sc = make_sched(p, row0, row1, hA, 2);
   const int t_begin = (int)((int64_t)sc.total * split / p.splits);
   const int nt = (int)((int64_t)sc.total * (split + 1) / p.splits) - t_begin;
   const PairFills fl{max(0, min(sc.n_contig - t_begin, nt))};
@@ -992,6 +1029,11 @@ int make_map(CUtensorMap* m, int* swap, const void* base, int dtype, int64_t hea
   return BB_OK;
 }
 
+// Bytes of one of the two gathered routed-row arrays.
+size_t gather_kv_bytes(const bb_flash_args* a) {
+  return align_up((size_t)a->bh * a->route_groups * cdiv(a->route_k, BN) * BN * 128 * 2, 256);
+}
+
 template <typename T>
 int launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream) {
   p.serial = unit_next_serial();
@@ -1011,6 +1053,11 @@ int launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream) {
   if (p.kg) {
     const int64_t rows = p.bh * p.route_groups * p.route_kpad;
     if (rows > 0x7fffffffLL) return fail(BB_ERR_UNSUPPORTED, "flash: too many routed rows (%lld)", (long long)rows);
+    const size_t half = gather_kv_bytes(a);
+    p.vg = static_cast<char*>(p.kg) + half;
+    p.tile_min = reinterpret_cast<int32_t*>(static_cast<char*>(p.vg) + half);
+    if (cudaMemsetAsync(p.tile_min, 0xff, (size_t)(rows / BN) * 4, stream) != cudaSuccess)
+      return fail(BB_ERR_LAUNCH, "flash: %s", cudaGetErrorString(cudaGetLastError()));
     int unused = 0;
     st = make_map(&maps.kg, &unused, p.kg, a->dtype, 1, rows, 0, 128);
     if (st) return st;
@@ -1062,7 +1109,7 @@ int flash_tc_splits(const bb_flash_args* a, int sms) {
 
 size_t flash_tc_gather_bytes(const bb_flash_args* a) {
   if (a->route_k <= 0) return 0;
-  return 2 * align_up((size_t)a->bh * a->route_groups * cdiv(a->route_k, tc::BN) * tc::BN * 128 * 2, 256);
+  return 2 * tc::gather_kv_bytes(a) + align_up((size_t)a->bh * a->route_groups * cdiv(a->route_k, tc::BN) * 4, 256);
 }
 
 int flash_tc_launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream) {
