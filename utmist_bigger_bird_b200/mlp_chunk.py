@@ -34,10 +34,10 @@ def _is_swiglu(mlp) -> bool:
 
 
 def _swiglu_chunked(mlp, chunk: int, base):
-    def forward(x, _mlp=mlp, _base=base):
+    def forward(x):
         if not x.is_cuda:
-            return _generic(_base, chunk)(x)
-        wg, wu, wd = _mlp.gate_proj.weight, _mlp.up_proj.weight, _mlp.down_proj.weight
+            return _generic(base, chunk)(x)
+        wg, wu, wd = mlp.gate_proj.weight, mlp.up_proj.weight, mlp.down_proj.weight
         n = x.shape[-2]
         step = chunk if 0 < chunk < n else n
         lead = x.shape[:-2]
@@ -61,20 +61,28 @@ def _swiglu_chunked(mlp, chunk: int, base):
                 torch.matmul(g, wd.t(), out=dst)
             else:
                 dst.copy_(torch.matmul(g, wd.t()))
-        reduce = getattr(_mlp.down_proj, "all_reduce_", None)  # tensor-parallel down projection
+        reduce = getattr(mlp.down_proj, "all_reduce_", None)  # tensor-parallel down projection
         return reduce(out) if reduce is not None else out
 
     return forward
 
 
 def _generic(base, chunk: int):
-    def forward(x, _base=base):
+    """``base`` over consecutive token slices of at most ``chunk`` rows, written into one output
+    buffer whose trailing size comes from the first slice's result."""
+    def forward(x):
         n = x.shape[-2]
         if n <= chunk:
-            return _base(x)
-        out = torch.empty_like(x)
-        for s in range(0, n, chunk):
-            out[..., s:s + chunk, :] = _base(x[..., s:s + chunk, :])
+            return base(x)
+        pieces = x.split(chunk, dim=-2)
+        head = base(pieces[0])
+        out = head.new_empty((*head.shape[:-2], n, head.shape[-1]))
+        out.narrow(-2, 0, head.shape[-2]).copy_(head)
+        done = head.shape[-2]
+        del head
+        for piece in pieces[1:]:
+            out.narrow(-2, done, piece.shape[-2]).copy_(base(piece))
+            done += piece.shape[-2]
         return out
 
     return forward
