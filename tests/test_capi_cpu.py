@@ -82,13 +82,15 @@ def test_flash_workspace_sizes():
     L = _lib.lib()
     nbytes = C.c_size_t(0)
     # main pass of the 128K layer: plenty of CTAs, no key split; the workspace holds only the routed
-    # K and V rows gathered once per call ([bh, groups, route_k rounded up to 128, d] bf16 each)
+    # K and V rows gathered once per call ([bh, groups, route_k rounded up to 128, d] bf16 each) and
+    # each 128-slot routed tile's smallest position (int32, the area rounded up to 256 bytes)
     a = _flash_args(t=131072, n=131072, window=16384, route_k=512, route_chunk=131072, row_end=131072 - 256)
+    want = 2 * a.bh * a.route_groups * 512 * 128 * 2 + -(-a.bh * a.route_groups * 4 * 4 // 256) * 256
     assert L.bb_flash_workspace_size(C.byref(a), C.byref(nbytes)) == 0
-    assert nbytes.value == 2 * a.bh * a.route_groups * 512 * 128 * 2
+    assert nbytes.value == want
     a.route_k = 500  # padded to whole 128-slot tiles
     assert L.bb_flash_workspace_size(C.byref(a), C.byref(nbytes)) == 0
-    assert nbytes.value == 2 * a.bh * a.route_groups * 512 * 128 * 2
+    assert nbytes.value == want
     a.d, a.route_k = 64, 512  # head_dim 64 runs on the mma.sync kernel, which gathers in-kernel
     assert L.bb_flash_workspace_size(C.byref(a), C.byref(nbytes)) == 0 and nbytes.value == 0
     # exact tail: 256 rows over 128K keys split across the machine -> partials workspace
