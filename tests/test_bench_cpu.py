@@ -1,5 +1,5 @@
 """Host logic of bench.py that runs without a GPU: the per-rank share option, the scope of the main
-kernel's DRAM-traffic figure and the CPU description."""
+kernel's DRAM-traffic figure, the CPU description and the CPU leg."""
 import pytest
 
 import bench
@@ -45,3 +45,10 @@ def test_sources_hash_is_stable():
 
 def test_cpu_model_is_named():
     assert isinstance(bench.cpu_model(), str) and bench.cpu_model()
+
+
+def test_cpu_leg_runs_and_counts_flops():
+    """The CPU leg (the torch restatement that --impl reference and cpu_baseline time) on config 1:
+    it runs on the CPU and reports positive seconds and FLOPs."""
+    dt, flops = bench.cpu_sample(CONFIGS["config1"], rows_per_head=12)
+    assert dt > 0 and flops > 0
