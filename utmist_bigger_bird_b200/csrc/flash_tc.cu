@@ -822,12 +822,10 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
         ok = false;
         break;
       }
-      // P_w(j-1) V_{j-1} was issued before S_w(j), so it has completed by now (in-order tensor
-      // pipe): this wait returns at once and keeps the O barrier's phases in step.
-      if (j > 0 && !mbar_wait_warp(bar(PB_O + w), (j - 1) & 1, abort_flag, F_SOFTMAX_O)) {
-        ok = false;
-        break;
-      }
+      // P_w(j-1) V_{j-1} was issued before S_w(j), and the commit that completed S_w(j) tracks every
+      // earlier MMA of the issuer, so O(j-1) is complete now (the rescale below may read it). The O
+      // barrier is therefore waited only once, for the last tile: it is then at most one phase
+      // behind, which a parity wait resolves.
       tc_fence_after();
       // The whole S row in registers (one TMEM load), its exact max, then P = exp2(s * c - m_ref)
       // written as packed 16-bit pairs over S columns [0, 64) in four 16-column stores.
