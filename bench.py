@@ -42,9 +42,9 @@ KERNEL_SOURCES = [ROOT / "utmist_bigger_bird_b200" / "csrc" / f for f in ("flash
 # DRAM traffic of the main-pass kernel, from one ncu capture (dram__bytes_read.sum +
 # dram__bytes_write.sum) of config 2's main pass, and the hash of the kernel sources it was taken
 # on. When the sources change the figure no longer describes the kernel and the bench reports null.
-MAIN_TRAFFIC = {"sources_sha256": "a27f5f4362a1a5be", "bytes_per_launch": 643.43e6 * (131072 - 256) / (32768 - 256),
+MAIN_TRAFFIC = {"sources_sha256": "18e0b6d7a88f7e36", "bytes_per_launch": 642.36e6 * (131072 - 256) / (32768 - 256),
                 "capture": "dram__bytes_read.sum + dram__bytes_write.sum of the main pass of "
-                           "`bench.py --config sweep_n32768_w16384 --part layer` (643.4 MB), scaled by main-pass "
+                           "`bench.py --config sweep_n32768_w16384 --part layer` (642.4 MB), scaled by main-pass "
                            "query rows x4.024"}
 
 
