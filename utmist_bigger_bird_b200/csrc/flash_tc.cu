@@ -45,6 +45,36 @@ constexpr int THREADS = 192;
 constexpr int NB = 4;
 constexpr float RESCALE_LOG2 = 8.0f;
 
+// In the pair kernel's softmax every EXP2_POLY_EVERY-th pair of exponentials of a row is computed on
+// the FMA pipe (exp2_poly2) instead of the special-function unit, so the two pipes share the row's
+// exponentials.
+constexpr int EXP2_POLY_EVERY = 8;
+
+// 2^x of a packed pair on the FMA pipe, x = j + f with j = floor(x) and f in [0, 1): adding 1.5 * 2^23
+// rounded toward minus infinity leaves j in the low mantissa bits of t, 2^f comes from a degree-3
+// polynomial with p(0) = 1 fitted here for minimax relative error on [0, 1) (8.6e-5, below the
+// rounding step of the 16-bit P it feeds), and 2^j is added into p's exponent field (t's bits shifted
+// left by 23 are j << 23, since every higher bit of t shifts out). x is clamped at -127, where f = 0
+// and p = 1, so the sum clears the exponent field exactly: scores that far below the reference (and
+// masked ones, -inf) give exactly 0, as the special-function unit's flush-to-zero exponential does.
+// x = 0 gives exactly 1; x never exceeds the lazy-rescale bound, far inside the exponent range.
+__device__ __forceinline__ void exp2_poly2(uint64_t x2, float& a, float& b) {
+  float xa, xb;
+  f2_unpack(x2, xa, xb);
+  const uint64_t xc = f2_pack(fmaxf(xa, -127.f), fmaxf(xb, -127.f));
+  const uint64_t big = f2_pack(12582912.f, 12582912.f);
+  const uint64_t t = f2_add_rm(xc, big);
+  const uint64_t fr = f2_sub(xc, f2_sub(t, big));
+  uint64_t p = f2_fma(f2_pack(0.07706707f, 0.07706707f), fr, f2_pack(0.22764495f, 0.22764495f));
+  p = f2_fma(p, fr, f2_pack(0.6951168f, 0.6951168f));
+  p = f2_fma(p, fr, f2_pack(1.f, 1.f));
+  float pa, pb, ta, tb;
+  f2_unpack(p, pa, pb);
+  f2_unpack(t, ta, tb);
+  a = __uint_as_float(__float_as_uint(pa) + (__float_as_uint(ta) << 23));
+  b = __uint_as_float(__float_as_uint(pb) + (__float_as_uint(tb) << 23));
+}
+
 constexpr uint32_t SM_Q = 0;
 constexpr uint32_t SM_KV = TILE;
 enum { B_Q = 0, B_FULL = 1, B_EMPTY = B_FULL + NB, B_S = B_EMPTY + NB, B_P = B_S + 2, B_O = B_P + 2,
@@ -563,11 +593,19 @@ __global__ void __launch_bounds__(THREADS, 1) flash_tc_kernel(const __grid_const
 //   S_A = columns 0-127, S_B = 128-255, O_A = 256-383, O_B = 384-511.
 // The single MMA thread alternates  P_A V -> S_A(next) -> P_B V -> S_B(next), so while one
 // warpgroup runs its softmax the tensor core works for the other (ping-pong).
-// 320 threads (10 warps; at most 3 warps share an SM sub-partition's 16K registers, so 168
-// registers per thread): producer (warp 0), MMA issuer (warp 1),
-// softmax of head A (warps 2-5) and of head B (warps 6-9); warp w reads TMEM lanes
-// 32 * (w % 4) .. 32 * (w % 4) + 31, so each softmax group covers all 128 rows.
-constexpr int P_THREADS = 320;
+// 384 threads (12 warps, three per SM sub-partition): warpgroup 0 = producer (warp 0), MMA issuer
+// (warp 1) and two idle warps; softmax of head A (warps 4-7) and of head B (warps 8-11), with more
+// registers than the launch gives (P_REG_HIGH below) for the score row and its exponentials; warp w
+// reads TMEM lanes 32 * (w % 4) .. 32 * (w % 4) + 31, so each softmax group covers all 128 rows.
+constexpr int P_THREADS = 384;
+// Register split (setmaxnreg): the launch gives every thread P_REG_LAUNCH registers (what ptxas
+// reports for this kernel); warpgroup 0 (producer, MMA issuer, two idle warps) drops to P_REG_LOW so
+// that the two softmax warpgroups can rise to P_REG_HIGH. The shares must add up to at most the
+// launch total (an increase waits for registers that a decrease frees), and every SM sub-partition
+// holds one warp of each warpgroup.
+constexpr int P_REG_LAUNCH = 168, P_REG_LOW = 104, P_REG_HIGH = 200;
+static_assert(128 * P_REG_LOW + 256 * P_REG_HIGH <= P_THREADS * P_REG_LAUNCH, "register split exceeds the launch");
+static_assert(32 * (P_REG_LOW + 2 * P_REG_HIGH) <= 16384, "register split exceeds a sub-partition");
 // K/V ring: 5 slots of 32 KB, the most that fits beside the two Q tiles in 227 KB. Fill order:
 // a shared step loads K_j then V_j (two fills), a routed step K_A, K_B, V_A, V_B (four fills). At
 // most four filled slots are in use at once (V_A, V_B of the previous step and K_A, K_B of this
@@ -640,7 +678,8 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
   tc_fence_after();
   const uint32_t tmem = misc[0];
 
-  if (warp < 2) {
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(P_REG_LOW));
     if (warp == 0) {
       // ---------------------------------------------------------------- producer
       int fills[PNB];
@@ -801,7 +840,8 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
-    const int w = (warp - 2) >> 2;  // 0: head A, 1: head B
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(P_REG_HIGH));
+    const int w = (warp - 4) >> 2;  // 0: head A (warps 4-7), 1: head B (warps 8-11)
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const int64_t h = hA + w;
@@ -866,9 +906,16 @@ __global__ void __launch_bounds__(P_THREADS, 1) flash_tc_pair_kernel(const __gri
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float xa, xb;
-          f2_unpack(f2_fma(f2_pack(s[32 * q + 2 * i], s[32 * q + 2 * i + 1]), c2, n2), xa, xb);
-          const float a = fast_exp2(xa), b = fast_exp2(xb);
+          const uint64_t x2 = f2_fma(f2_pack(s[32 * q + 2 * i], s[32 * q + 2 * i + 1]), c2, n2);
+          float a, b;
+          if (i % EXP2_POLY_EVERY == EXP2_POLY_EVERY - 1) {
+            exp2_poly2(x2, a, b);
+          } else {
+            float xa, xb;
+            f2_unpack(x2, xa, xb);
+            a = fast_exp2(xa);
+            b = fast_exp2(xb);
+          }
           ls[i & 3] += a + b;
           pk[i] = pack2<T>(a, b);
         }
@@ -1066,6 +1113,18 @@ int launch(const bb_flash_args* a, FlashParams& p, cudaStream_t stream) {
     BB_CHECK_LAUNCH("route_gather_kernel");
   }
   if (pair_mode(a)) {
+    // The kernel's register split only works if the launch hands out at least what its warpgroups
+    // ask for; an increase beyond that would wait forever, so refuse to launch instead.
+    static int launch_regs = -1;
+    if (launch_regs < 0) {
+      cudaFuncAttributes fa{};
+      if (cudaFuncGetAttributes(&fa, flash_tc_pair_kernel<T>) != cudaSuccess)
+        return fail(BB_ERR_LAUNCH, "flash: %s", cudaGetErrorString(cudaGetLastError()));
+      launch_regs = fa.numRegs;
+    }
+    if (launch_regs * P_THREADS < 128 * P_REG_LOW + 256 * P_REG_HIGH)
+      return fail(BB_ERR_LAUNCH, "flash: the pair kernel launches with %d registers a thread, fewer than its split needs",
+                  launch_regs);
     cudaFuncSetAttribute(flash_tc_pair_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SM_ALLOC);
     dim3 grid((unsigned)cdiv(a->row_end - a->row_begin, BM), (unsigned)(a->bh / 2), (unsigned)p.splits);
     flash_tc_pair_kernel<T><<<grid, P_THREADS, P_SM_ALLOC, stream>>>(maps, p);
