@@ -42,9 +42,9 @@ KERNEL_SOURCES = [ROOT / "utmist_bigger_bird_b200" / "csrc" / f for f in ("flash
 # DRAM traffic of the main-pass kernel, from one ncu capture (dram__bytes_read.sum +
 # dram__bytes_write.sum) of config 2's main pass, and the hash of the kernel sources it was taken
 # on. When the sources change the figure no longer describes the kernel and the bench reports null.
-MAIN_TRAFFIC = {"sources_sha256": "3c6bcfc276de9c31", "bytes_per_launch": 647.47e6 * (131072 - 256) / (32768 - 256),
+MAIN_TRAFFIC = {"sources_sha256": "21f28c8d45ed1775", "bytes_per_launch": 644.84e6 * (131072 - 256) / (32768 - 256),
                 "capture": "dram__bytes_read.sum + dram__bytes_write.sum of the main pass of "
-                           "`bench.py --config sweep_n32768_w16384 --part layer` (647.5 MB), scaled by main-pass "
+                           "`bench.py --config sweep_n32768_w16384 --part layer` (644.8 MB), scaled by main-pass "
                            "query rows x4.024"}
 
 

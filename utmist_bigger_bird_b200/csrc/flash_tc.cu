@@ -1152,10 +1152,14 @@ int flash_tc_splits(const bb_flash_args* a, int sms) {
   const int64_t tiles = cdiv(std::min(a->n, a->window + tc::BM), tc::BN) + cdiv(a->front, tc::BN) +
                         cdiv(a->route_k, tc::BN);
   if (ctas <= 0 || ctas >= 2LL * sms || tiles < 16) return 1;
+  // Cost of s splits in key-tile steps: whole waves of CTAs times each CTA's steps plus its fixed
+  // cost (start-up to the first S, epilogue, the partial-result write and its share of the combine),
+  // which timings of the exact tail over explicit split counts put at about ten steps.
+  constexpr int64_t CTA_FIXED_STEPS = 10;
   int best = 1;
-  int64_t best_cost = cdiv(ctas, sms) * tiles;
+  int64_t best_cost = cdiv(ctas, sms) * (tiles + CTA_FIXED_STEPS);
   for (int s = 2; s <= 32 && s * 4 <= tiles; ++s) {
-    const int64_t cost = cdiv(ctas * s, sms) * cdiv(tiles, s) + 2;  // +2: split overhead
+    const int64_t cost = cdiv(ctas * s, sms) * (cdiv(tiles, s) + CTA_FIXED_STEPS);
     if (cost < best_cost) {
       best_cost = cost;
       best = s;
