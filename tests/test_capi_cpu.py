@@ -93,9 +93,15 @@ def test_flash_workspace_sizes():
     assert nbytes.value == want
     a.d, a.route_k = 64, 512  # head_dim 64 runs on the mma.sync kernel, which gathers in-kernel
     assert L.bb_flash_workspace_size(C.byref(a), C.byref(nbytes)) == 0 and nbytes.value == 0
-    # exact tail: 256 rows over 128K keys split across the machine -> partials workspace
-    a = _flash_args(t=256, n=131072, front=0, window=131072, route_k=0, route_chunk=131072, row_end=256)
-    assert L.bb_flash_workspace_size(C.byref(a), C.byref(nbytes)) == 0 and nbytes.value > 0
+    # exact tail: 256 rows over n keys split across the machine -> partials workspace of
+    # [splits, bh, t, 128] fp32 plus [splits, bh, t] (max, sum) pairs. The split count minimises whole
+    # waves of CTAs (148 SMs without a GPU) times each CTA's key tiles plus ~10 tiles of fixed cost:
+    # 9 at 128K (288 CTAs, 2 waves of 114 + 10), 4 at 32K (128 CTAs, 1 wave of 64 + 10).
+    for n, splits in ((131072, 9), (32768, 4)):
+        a = _flash_args(t=256, n=n, front=0, window=n, route_k=0, route_chunk=n, row_end=256)
+        want = splits * a.bh * 256 * 128 * 4 + splits * a.bh * 256 * 8
+        assert L.bb_flash_workspace_size(C.byref(a), C.byref(nbytes)) == 0
+        assert nbytes.value == want, (n, nbytes.value, want)
 
 
 def test_routes_host_validation():
